@@ -1,0 +1,431 @@
+// Binning on sm_100a: duplicate-with-keys, a stable LSD onesweep radix sort of
+// the (tile | depth) keys, and tile ranges / bucket counts.
+//
+// Duplicate follows fastgs_core/metal/fastgs_binning.metal:182-213 (the tile
+// walk itself is tile_walk.cuh). The sort replaces mx::argsort + mx::take
+// (fastgs_core/binding/binding.cpp:195-197) with a hand-written onesweep LSD
+// radix sort over 8-bit digits of the significant bits only: one histogram
+// pass over the keys computes every digit histogram, then each digit pass
+// reads and writes the pairs once (24 B per key per pass), ranking keys in a
+// CTA with warp match/popc multi-split and resolving the CTA's global digit
+// offsets by a decoupled look-back over earlier CTAs. Look-back waits are
+// bounded: after kSpinLimit polls a CTA flags FGS_ERR_TIMEOUT, stops waiting
+// and clamps its stores to the output. Tile ranges follow
+// fastgs_core/metal/fastgs_tile_prep.metal:10-53.
+#include <cstdio>
+
+#include "../../include/fastgs_b200.h"
+#include "fgs_common.cuh"
+#include "tile_walk.cuh"
+
+namespace fgs {
+
+// ---------------------------------------------------------------- duplicate
+constexpr int kDupThreads = 256;
+
+__global__ void __launch_bounds__(kDupThreads)
+    duplicate_kernel(int n, float mult, int gx, int gy, const float2* __restrict__ xys,
+                     const float* __restrict__ depths, const uint32_t* __restrict__ offsets,
+                     const float4* __restrict__ conic, const uint32_t* __restrict__ tiles,
+                     int64_t num_rendered, uint64_t* __restrict__ keys,
+                     uint32_t* __restrict__ values) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t cnt = tiles[i];
+  if (cnt == 0u) return;
+  const int64_t off0 = (i == 0) ? 0 : (int64_t)offsets[i - 1];
+  const uint64_t dbits = (uint64_t)__float_as_uint(depths[i]);
+  const float2 p = xys[i];
+  int64_t off = off0;
+  const int64_t end = off0 + cnt;
+  tile_walk(p.x, p.y, conic[i], gx, gy, mult, [&](int tile) {
+    if (off < end && off < num_rendered) {
+      keys[off] = ((uint64_t)(int64_t)tile << 32) | dbits;
+      values[off] = (uint32_t)i;
+    }
+    ++off;
+  });
+  // The reference's zero-filled outputs leave any slot the walk did not reach
+  // at (key 0, value 0); write that explicitly.
+  for (; off < end && off < num_rendered; ++off) {
+    keys[off] = 0ull;
+    values[off] = 0u;
+  }
+}
+
+// --------------------------------------------------------------------- sort
+constexpr int kRadix = 256;
+constexpr int kSortThreads = 256;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortItems = 15;
+constexpr int kPart = kSortThreads * kSortItems;  // keys per partition (3840)
+constexpr int kMaxPasses = 8;
+constexpr uint32_t kFlagAgg = 1u << 30;
+constexpr uint32_t kFlagPrefix = 2u << 30;
+constexpr uint32_t kValueMask = (1u << 30) - 1u;
+constexpr int kSpinLimit = 1 << 22;
+constexpr int kSortDynSmem = kPart * (8 + 4);
+
+struct SortWs {
+  uint32_t* hist;       // [passes][256] global digit counts -> exclusive offsets
+  uint32_t* lookback;   // [passes][parts][256]
+  uint32_t* counters;   // [passes] partition tickets
+  int* err;             // timeout flag
+  uint64_t* tmp_keys;
+  uint32_t* tmp_vals;
+};
+
+__global__ void __launch_bounds__(256)
+    sort_histogram_kernel(const uint64_t* __restrict__ keys, int64_t n, int passes,
+                          uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_h[kMaxPasses][kRadix];
+  for (int k = threadIdx.x; k < kMaxPasses * kRadix; k += blockDim.x) (&s_h[0][0])[k] = 0u;
+  __syncthreads();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint64_t k = keys[i];
+    for (int p = 0; p < passes; ++p) atomicAdd(&s_h[p][(k >> (8 * p)) & 0xffu], 1u);
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < passes * kRadix; k += blockDim.x) {
+    const uint32_t v = (&s_h[0][0])[k];
+    if (v) atomicAdd(hist + k, v);
+  }
+}
+
+// exclusive scan of each pass's 256 digit counts (one CTA per pass)
+__global__ void __launch_bounds__(kRadix) sort_hist_scan_kernel(uint32_t* hist) {
+  __shared__ uint32_t s_w[kRadix / 32];
+  uint32_t* h = hist + blockIdx.x * kRadix;
+  const uint32_t v = h[threadIdx.x];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_w[w] = x;
+  __syncthreads();
+  uint32_t add = 0;
+  for (int k = 0; k < w; ++k) add += s_w[k];
+  h[threadIdx.x] = x - v + add;
+}
+
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+    onesweep_kernel(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+                    uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
+                    int shift, const uint32_t* __restrict__ digit_offsets,
+                    uint32_t* __restrict__ lookback, uint32_t* __restrict__ counter,
+                    int* __restrict__ err) {
+  __shared__ uint32_t s_part;
+  __shared__ uint32_t s_whist[kSortWarps][kRadix];  // per-warp digit counts -> warp offsets
+  __shared__ uint32_t s_local_start[kRadix];
+  __shared__ uint32_t s_global_base[kRadix];
+  __shared__ uint32_t s_wsum[kSortWarps];
+  extern __shared__ __align__(16) unsigned char s_dyn[];
+  uint64_t* s_keys = reinterpret_cast<uint64_t*>(s_dyn);       // [kPart]
+  uint32_t* s_vals = reinterpret_cast<uint32_t*>(s_keys + kPart);  // [kPart]
+
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) s_part = atomicAdd(counter, 1u);
+  for (int k = tid; k < kSortWarps * kRadix; k += kSortThreads) (&s_whist[0][0])[k] = 0u;
+  __syncthreads();
+  const uint32_t part = s_part;
+  const int64_t base = (int64_t)part * kPart;
+  const int valid = (int)((int64_t)kPart < n - base ? (int64_t)kPart : n - base);
+
+  // warp-striped load: warp w owns [w*32*I, (w+1)*32*I), item i of lane l is +i*32+l
+  uint64_t k[kSortItems];
+  uint32_t v[kSortItems];
+  uint32_t r[kSortItems];
+#pragma unroll
+  for (int i = 0; i < kSortItems; ++i) {
+    const int li = w * 32 * kSortItems + i * 32 + lane;
+    if (li < valid) {
+      k[i] = keys_in[base + li];
+      v[i] = vals_in[base + li];
+    } else {
+      k[i] = ~0ull;  // pads: digit 255, ranked after every real key of the partition
+      v[i] = 0u;
+    }
+  }
+  const uint32_t lt_mask = (1u << lane) - 1u;
+#pragma unroll
+  for (int i = 0; i < kSortItems; ++i) {
+    const uint32_t d = (uint32_t)(k[i] >> shift) & 0xffu;
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const uint32_t before = s_whist[w][d];
+    __syncwarp();
+    if (lane == (__ffs(peers) - 1)) s_whist[w][d] = before + __popc(peers);
+    __syncwarp();
+    r[i] = before + __popc(peers & lt_mask);
+  }
+  __syncthreads();
+  // thread d: warp offsets within the digit and the CTA's digit count
+  const uint32_t d = tid;
+  uint32_t cnt = 0;
+#pragma unroll
+  for (int ww = 0; ww < kSortWarps; ++ww) {
+    const uint32_t c = s_whist[ww][d];
+    s_whist[ww][d] = cnt;
+    cnt += c;
+  }
+  const uint32_t pads = (uint32_t)(kPart - valid);
+  const uint32_t real_cnt = (d == kRadix - 1) ? cnt - pads : cnt;
+  // publish this partition's aggregate as early as possible
+  uint32_t* lb = lookback + (size_t)part * kRadix + d;
+  if (part == 0)
+    st_volatile(lb, kFlagPrefix | real_cnt);
+  else
+    st_volatile(lb, kFlagAgg | real_cnt);
+  // CTA-local exclusive scan over digits (for the shared-memory sort)
+  {
+    uint32_t x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_wsum[w] = x;
+    __syncthreads();
+    uint32_t add = 0;
+    for (int ww = 0; ww < w; ++ww) add += s_wsum[ww];
+    s_local_start[d] = x - cnt + add;
+  }
+  // decoupled look-back over earlier partitions for digit d
+  uint32_t excl = 0;
+  if (part > 0) {
+    int64_t j = (int64_t)part - 1;
+    int spins = 0;
+    while (j >= 0) {
+      const uint32_t s = ld_volatile(lookback + (size_t)j * kRadix + d);
+      const uint32_t flag = s & ~kValueMask;
+      if (flag == 0u) {
+        if (++spins > kSpinLimit) {
+          atomicExch(err, 1);
+          break;
+        }
+        __nanosleep(32);
+        continue;
+      }
+      excl += s & kValueMask;
+      if (flag == kFlagPrefix) break;
+      --j;
+    }
+    st_volatile(lb, kFlagPrefix | ((excl + real_cnt) & kValueMask));
+  }
+  s_global_base[d] = digit_offsets[d] + excl;
+  __syncthreads();
+  // scatter into shared memory in digit order (stable)
+#pragma unroll
+  for (int i = 0; i < kSortItems; ++i) {
+    const uint32_t dd = (uint32_t)(k[i] >> shift) & 0xffu;
+    const uint32_t pos = s_local_start[dd] + s_whist[w][dd] + r[i];
+    s_keys[pos] = k[i];
+    s_vals[pos] = v[i];
+  }
+  __syncthreads();
+  for (int j = tid; j < valid; j += kSortThreads) {
+    const uint64_t key = s_keys[j];
+    const uint32_t dd = (uint32_t)(key >> shift) & 0xffu;
+    const uint64_t dst = (uint64_t)s_global_base[dd] + (uint64_t)(j - (int)s_local_start[dd]);
+    if (dst < (uint64_t)n) {
+      keys_out[dst] = key;
+      vals_out[dst] = s_vals[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- tile prep
+__global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, int64_t n, int num_tiles,
+                                   uint32_t* __restrict__ ranges) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  const uint32_t cur = (uint32_t)(keys[g] >> 32);
+  const bool valid = cur != 0xffffffffu;
+  if (g == 0) {
+    if (cur < (uint32_t)num_tiles) ranges[2 * (size_t)cur] = 0u;
+  } else {
+    const uint32_t prev = (uint32_t)(keys[g - 1] >> 32);
+    if (cur != prev) {
+      if (prev < (uint32_t)num_tiles) ranges[2 * (size_t)prev + 1] = (uint32_t)g;
+      if (valid && cur < (uint32_t)num_tiles) ranges[2 * (size_t)cur] = (uint32_t)g;
+    }
+  }
+  if (g == n - 1 && valid && cur < (uint32_t)num_tiles) ranges[2 * (size_t)cur + 1] = (uint32_t)n;
+}
+
+// one CTA: bucket counts, their inclusive scan and the total
+__global__ void __launch_bounds__(1024)
+    bucket_count_kernel(const uint32_t* __restrict__ ranges, int num_tiles,
+                        uint32_t* __restrict__ bucket_count, uint32_t* __restrict__ bucket_offsets,
+                        uint64_t* __restrict__ bucket_sum) {
+  __shared__ uint32_t s_w[32];
+  __shared__ uint32_t s_carry;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int base = 0; base < num_tiles; base += 1024) {
+    const int t = base + threadIdx.x;
+    uint32_t c = 0;
+    if (t < num_tiles) {
+      const int ns = (int)(ranges[2 * t + 1] - ranges[2 * t]);
+      c = (uint32_t)((ns + 31) / 32);
+      bucket_count[t] = c;
+    }
+    uint32_t x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) s_w[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      uint32_t s = s_w[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      s_w[lane] = s;
+    }
+    __syncthreads();
+    if (t < num_tiles) bucket_offsets[t] = s_carry + x + (w > 0 ? s_w[w - 1] : 0u);
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += s_w[31];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *bucket_sum = s_carry;
+}
+
+static inline int sort_passes(int key_bits) { return (key_bits + 7) / 8; }
+static inline int64_t sort_parts(int64_t n) { return (n + kPart - 1) / kPart; }
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace fgs
+
+using namespace fgs;
+
+extern "C" {
+
+int fgs_duplicate_with_keys(int32_t n, float mult, int32_t tile_bounds_x, int32_t tile_bounds_y,
+                            const float* xys, const float* depths, const uint32_t* point_offsets,
+                            const float* conic_opacity, const uint32_t* tiles_touched,
+                            int64_t num_rendered, uint64_t* keys_unsorted,
+                            uint32_t* values_unsorted, void* stream) {
+  FGS_CHECK_ARG(n >= 0 && num_rendered >= 0, "sizes must be >= 0");
+  if (n == 0 || num_rendered == 0) return FGS_OK;
+  FGS_CHECK_ARG(xys && depths && point_offsets && conic_opacity && tiles_touched && keys_unsorted &&
+                    values_unsorted,
+                "missing pointer");
+  FGS_CHECK_ARG(tile_bounds_x > 0 && tile_bounds_y > 0, "tile bounds must be positive");
+  duplicate_kernel<<<(n + kDupThreads - 1) / kDupThreads, kDupThreads, 0, (cudaStream_t)stream>>>(
+      n, mult, tile_bounds_x, tile_bounds_y, (const float2*)xys, depths, point_offsets,
+      (const float4*)conic_opacity, tiles_touched, num_rendered, keys_unsorted, values_unsorted);
+  return check_launch("duplicate_with_keys");
+}
+
+size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits) {
+  const int passes = sort_passes(key_bits);
+  const int64_t parts = sort_parts(num_rendered > 0 ? num_rendered : 1);
+  size_t b = 0;
+  b += align256((size_t)passes * kRadix * 4);               // hist
+  b += align256((size_t)passes * parts * kRadix * 4);       // lookback
+  b += align256((size_t)passes * 4);                        // counters
+  b += align256(4);                                         // err
+  b += align256((size_t)(num_rendered > 0 ? num_rendered : 1) * 8);  // tmp keys
+  b += align256((size_t)(num_rendered > 0 ? num_rendered : 1) * 4);  // tmp vals
+  return b;
+}
+
+int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,
+                   const uint32_t* values_in, uint64_t* keys_out, uint32_t* values_out,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  FGS_CHECK_ARG(num_rendered >= 0, "num_rendered must be >= 0");
+  FGS_CHECK_ARG(key_bits >= 1 && key_bits <= 64, "key_bits must be in [1, 64]");
+  if (num_rendered == 0) return FGS_OK;
+  if (num_rendered > (int64_t)kValueMask) {
+    fgs::set_error("sort supports at most %u keys, got %lld", kValueMask, (long long)num_rendered);
+    return FGS_ERR_CAPACITY;
+  }
+  const int passes = sort_passes(key_bits);
+  FGS_CHECK_ARG(passes <= kMaxPasses, "too many key bits");
+  FGS_CHECK_ARG(keys_in && values_in && keys_out && values_out && workspace, "missing pointer");
+  const size_t need = fgs_sort_workspace_bytes(num_rendered, key_bits);
+  FGS_CHECK_ARG(workspace_bytes >= need, "sort workspace too small: %zu < %zu", workspace_bytes, need);
+  const int64_t parts = sort_parts(num_rendered);
+  static bool attr_set = false;  // per process; the attribute is per function, all devices
+  if (!attr_set) {
+    cudaFuncSetAttribute(onesweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSortDynSmem);
+    attr_set = true;
+  }
+  char* w = (char*)workspace;
+  uint32_t* hist = (uint32_t*)w;
+  w += align256((size_t)passes * kRadix * 4);
+  uint32_t* lookback = (uint32_t*)w;
+  w += align256((size_t)passes * parts * kRadix * 4);
+  uint32_t* counters = (uint32_t*)w;
+  w += align256((size_t)passes * 4);
+  int* err = (int*)w;
+  w += align256(4);
+  uint64_t* tmp_keys = (uint64_t*)w;
+  w += align256((size_t)num_rendered * 8);
+  uint32_t* tmp_vals = (uint32_t*)w;
+  cudaStream_t s = (cudaStream_t)stream;
+  // hist .. err are contiguous: clear them in one memset
+  cudaMemsetAsync(hist, 0, (size_t)((char*)tmp_keys - (char*)hist), s);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t hb = (num_rendered + 4095) / 4096;
+  const int hblocks = (int)(hb < (int64_t)sms * 4 ? hb : (int64_t)sms * 4);
+  sort_histogram_kernel<<<hblocks > 0 ? hblocks : 1, 256, 0, s>>>(keys_in, num_rendered, passes, hist);
+  sort_hist_scan_kernel<<<passes, kRadix, 0, s>>>(hist);
+  const uint64_t* src_k = keys_in;
+  const uint32_t* src_v = values_in;
+  for (int p = 0; p < passes; ++p) {
+    // the last pass lands in the output buffers
+    const bool to_out = ((passes - 1 - p) % 2) == 0;
+    uint64_t* dk = to_out ? keys_out : tmp_keys;
+    uint32_t* dv = to_out ? values_out : tmp_vals;
+    onesweep_kernel<<<(unsigned)parts, kSortThreads, kSortDynSmem, s>>>(
+        src_k, src_v, dk, dv, num_rendered, 8 * p, hist + p * kRadix,
+        lookback + (size_t)p * parts * kRadix, counters + p, err);
+    src_k = dk;
+    src_v = dv;
+  }
+  return check_launch("sort_pairs");
+}
+
+int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorted_keys,
+                  uint32_t* ranges, uint32_t* bucket_count, uint32_t* bucket_offsets,
+                  uint64_t* bucket_sum, void* stream) {
+  FGS_CHECK_ARG(num_rendered >= 0 && num_tiles >= 0, "sizes must be >= 0");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (num_tiles == 0) {
+    if (bucket_sum) cudaMemsetAsync(bucket_sum, 0, 8, s);
+    return check_launch("tile_prep");
+  }
+  FGS_CHECK_ARG(ranges && bucket_count && bucket_offsets && bucket_sum, "missing pointer");
+  FGS_CHECK_ARG(num_rendered == 0 || sorted_keys, "missing keys");
+  cudaMemsetAsync(ranges, 0, (size_t)num_tiles * 2 * sizeof(uint32_t), s);
+  if (num_rendered > 0)
+    tile_ranges_kernel<<<(unsigned)((num_rendered + 255) / 256), 256, 0, s>>>(sorted_keys, num_rendered,
+                                                                              num_tiles, ranges);
+  bucket_count_kernel<<<1, 1024, 0, s>>>(ranges, num_tiles, bucket_count, bucket_offsets, bucket_sum);
+  return check_launch("tile_prep");
+}
+
+}  // extern "C"

@@ -1,0 +1,224 @@
+/*
+ * fastgs_b200.h - C ABI of the B200 (sm_100a) FastGS differentiable tile
+ * rasterizer: libfastgs_b200.so.
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer (cudaMalloc / torch CUDA
+ *     memory) unless its name ends in _host. Arrays are dense, row-major,
+ *     in the reference's layouts (float32 unless stated). Sizes are explicit.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). All work is
+ *     enqueued on it; nothing synchronises unless stated.
+ *   - Return value: FGS_OK (0) or an fgs_status code; fgs_last_error() gives a
+ *     message for the calling host thread. Invalid arguments are rejected
+ *     before anything is launched.
+ *   - Outputs are fully written: where the reference leaves an output at its
+ *     zero fill (culled Gaussians, unwritten bucket samples), these calls
+ *     write zeros, so callers need not clear them. Exceptions (accumulating
+ *     gradient outputs) say so.
+ *   - Tiles are 16x16 pixels; tile grid = ceil(W/16) x ceil(H/16).
+ *
+ * Each entry point names the reference interface it replaces
+ * (paths relative to the reference project a1091150/fastgs_core).
+ */
+#ifndef FASTGS_B200_H
+#define FASTGS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FGS_API __attribute__((visibility("default")))
+#else
+#define FGS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fgs_status {
+  FGS_OK = 0,
+  FGS_ERR_INVALID = 1,   /* bad shape / size / argument (reference: std::invalid_argument) */
+  FGS_ERR_CUDA = 2,      /* CUDA launch or runtime error */
+  FGS_ERR_TIMEOUT = 3,   /* a bounded device-side wait gave up (sort look-back) */
+  FGS_ERR_CAPACITY = 4,  /* a size exceeds what the call supports */
+};
+
+/* Message for the last failing call on this host thread ("" if none). */
+FGS_API const char* fgs_last_error(void);
+/* ABI version: 0x000100 = 0.1.0 */
+FGS_API int fgs_version(void);
+
+/* ---------------------------------------------------------------------------
+ * Preprocess forward.
+ * Replaces FastGSPreprocess (fastgs_core/include/fastgs_preprocess.h:13-55,
+ * fastgs_core/fastgs_preprocess.cpp:41-168) and the Metal kernel
+ * fastgs_preprocess_forward_kernel (fastgs_core/metal/fastgs_preprocess.metal:384-484).
+ * focal_x = W / (2 tan_fovx) as fastgs_preprocess.cpp:120-121.
+ */
+typedef struct fgs_preprocess_params {
+  int32_t n;                  /* Gaussians */
+  int32_t degree;             /* active SH degree 0..3 */
+  int32_t max_sh_coeffs;      /* sh.shape[1] (coefficients excluding DC) */
+  float scale_modifier;
+  float mult;                 /* FastGS opacity-aware extent multiplier */
+  float tan_fovx, tan_fovy;
+  int32_t image_width, image_height;
+  int32_t use_cov3d_precomp;  /* 1: cov3d_precomp path, 0: scales + quats */
+  int32_t use_colors_precomp; /* 1: colors_precomp path, 0: dc + sh */
+} fgs_preprocess_params;
+
+FGS_API int fgs_preprocess_forward(const fgs_preprocess_params* p,
+                           /* inputs */
+                           const float* means3d,        /* [n,3] */
+                           const float* dc,             /* [n,3]  (SH path) */
+                           const float* sh,             /* [n,max_sh_coeffs,3] */
+                           const float* colors_precomp, /* [n,3]  (colour path) */
+                           const float* opacities,      /* [n] */
+                           const float* scales,         /* [n,3] */
+                           const float* quats,          /* [n,4] (w,x,y,z) */
+                           const float* cov3d_precomp,  /* [n,6] */
+                           const float* viewmatrix,     /* [4,4] */
+                           const float* projmatrix,     /* [4,4] */
+                           const float* cam_pos,        /* [3] */
+                           const float* viewspace_in,   /* [n,4] */
+                           /* outputs */
+                           int32_t* radii,              /* [n] */
+                           float* xys,                  /* [n,2] */
+                           float* depths,               /* [n] */
+                           float* cov3d,                /* [n,6] */
+                           float* rgb,                  /* [n,3] */
+                           float* conic_opacity,        /* [n,4] */
+                           uint32_t* tiles_touched,     /* [n] */
+                           uint8_t* clamped,            /* [n,3] bool */
+                           float* viewspace_out,        /* [n,4] */
+                           void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Inclusive prefix sum of tiles_touched -> point_offsets, and its last
+ * element (num_rendered) into *total (device, uint64).
+ * Replaces mx::cumsum(tiles_touched) + read_last_u32
+ * (fastgs_core/binding/binding.cpp:153-154, :25-31). `scratch` holds
+ * fgs_scan_scratch_bytes(n) bytes of device memory.
+ */
+FGS_API size_t fgs_scan_scratch_bytes(int64_t n);
+FGS_API int fgs_inclusive_scan_u32(int64_t n, const uint32_t* in, uint32_t* out, uint64_t* total,
+                           void* scratch, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Duplicate with keys: key = (tile_id << 32) | float_bits(depth), value =
+ * Gaussian index, written from point_offsets[i-1].
+ * Replaces FastGSBinning (fastgs_core/include/fastgs_binning.h:13-34,
+ * fastgs_core/fastgs_binning.cpp:28-105) and
+ * fastgs_duplicate_with_keys_kernel (fastgs_core/metal/fastgs_binning.metal:182-213).
+ */
+FGS_API int fgs_duplicate_with_keys(int32_t n, float mult, int32_t tile_bounds_x, int32_t tile_bounds_y,
+                            const float* xys, const float* depths,
+                            const uint32_t* point_offsets, const float* conic_opacity,
+                            const uint32_t* tiles_touched, int64_t num_rendered,
+                            uint64_t* keys_unsorted, uint32_t* values_unsorted, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Stable LSD onesweep radix sort of (key, value) pairs on the low `key_bits`
+ * bits (32 depth bits + bits of the largest tile id). Inputs are not
+ * modified. Replaces mx::argsort + 2x mx::take (fastgs_core/binding/binding.cpp:195-197).
+ * `workspace` holds fgs_sort_workspace_bytes(num_rendered, key_bits) bytes.
+ * FGS_ERR_TIMEOUT if a bounded look-back wait gave up (the outputs are then
+ * undefined but every store stayed in bounds).
+ */
+FGS_API size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits);
+FGS_API int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,
+                   const uint32_t* values_in, uint64_t* keys_out, uint32_t* values_out,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Tile ranges [T,2] (empty tiles [0,0]) and per-tile bucket counts
+ * ceil(n_t / 32); plus, new here, the inclusive scan of bucket counts
+ * (per_tile_bucket_offset) and its total into *bucket_sum (device uint64).
+ * Replaces FastGSTilePrep (fastgs_core/include/fastgs_tile_prep.h:12-28,
+ * fastgs_core/fastgs_tile_prep.cpp:26-98; kernels
+ * fastgs_core/metal/fastgs_tile_prep.metal:10-53) and the bucket cumsum of
+ * fastgs_core/binding/binding.cpp:211-212.
+ */
+FGS_API int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorted_keys,
+                  uint32_t* ranges, uint32_t* bucket_count, uint32_t* bucket_offsets,
+                  uint64_t* bucket_sum, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rasterize forward: one CTA per 16x16 tile, front-to-back alpha blending
+ * with early termination, per-32-splat bucket samples for the backward pass.
+ * Replaces FastGSRasterize (fastgs_core/include/fastgs_rasterize.h:14-51,
+ * fastgs_core/fastgs_rasterize.cpp:32-168) and fastgs_render_forward_kernel
+ * (fastgs_core/metal/fastgs_rasterize.metal:25-159). sampled_ar is laid out
+ * [bucket][channel][256] as the reference writes it. metric_count is
+ * overwritten with this render's counts when get_flag != 0 (may be NULL
+ * otherwise). max_contrib is the max of n_contrib over in-image pixels.
+ */
+typedef struct fgs_raster_params {
+  int32_t image_width, image_height;
+  int32_t num_tiles;
+  int64_t bucket_sum;
+  int32_t num_gaussians;   /* size of metric_count */
+  int32_t get_flag;
+} fgs_raster_params;
+
+FGS_API int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
+                          const uint32_t* point_list, const uint32_t* bucket_offsets,
+                          const float* means2d, const float* colors, const float* conic_opacity,
+                          const float* background, const int32_t* metric_map,
+                          uint32_t* bucket_to_tile,  /* [bucket_sum] */
+                          float* sampled_t,          /* [bucket_sum*256] */
+                          float* sampled_ar,         /* [bucket_sum*3*256] */
+                          float* final_t,            /* [H*W] */
+                          uint32_t* n_contrib,       /* [H*W] */
+                          uint32_t* max_contrib,     /* [T] */
+                          float* pixel_colors,       /* [3,H*W] */
+                          float* out_color,          /* [3,H*W] */
+                          int32_t* metric_count,     /* [n] */
+                          void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rasterize backward (per-bucket: 32 splats x 256 pixels per warp).
+ * Replaces FastGSRasterizeBackward (fastgs_core/fastgs_rasterize_backward.cpp:35-166)
+ * and fastgs_render_backward_kernel (fastgs_core/metal/fastgs_rasterize_backward.metal:24-278).
+ * Gradients ACCUMULATE into dL_dmeans2d [n,2], dL_dcolors [n,3],
+ * dL_dconic_opacity [n,4], dL_dviewspace [n,4]; zero them first for a plain VJP.
+ */
+FGS_API int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
+                           const uint32_t* point_list, const uint32_t* bucket_offsets,
+                           const float* means2d, const float* colors, const float* conic_opacity,
+                           const float* background, const float* dL_dout_color,
+                           const uint32_t* bucket_to_tile, const float* sampled_t,
+                           const float* sampled_ar, const float* final_t,
+                           const uint32_t* n_contrib, const uint32_t* max_contrib,
+                           const float* pixel_colors, float* dL_dmeans2d, float* dL_dcolors,
+                           float* dL_dconic_opacity, float* dL_dviewspace, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Preprocess backward: conic -> cov2D -> (cov3D, means3D), projective
+ * Jacobian, SH backward with clamp mask, cov3D -> (scale, quat), identity for
+ * viewspace points. Outputs are written (not accumulated); rows of Gaussians
+ * with radii <= 0 are zero.
+ * Replaces FastGSPreprocessBackward (fastgs_core/fastgs_preprocess_backward.cpp:39-183)
+ * and fastgs_preprocess_backward_kernel
+ * (fastgs_core/metal/fastgs_preprocess_backward.metal:60-430).
+ * focal = 0.5 W / max(tan_fovx, 1e-6) as fastgs_preprocess_backward.cpp:134-137.
+ */
+FGS_API int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d,
+                            const float* scales, const float* quats, const float* viewmatrix,
+                            const float* projmatrix, const float* cam_pos, const float* sh,
+                            const float* cov3d_precomp, const float* cov3d_fwd,
+                            const float* dL_dcov3d,       /* [n,6] may be NULL (= 0) */
+                            const float* dL_drgb,         /* [n,3] */
+                            const float* dL_dxys,         /* [n,2] */
+                            const float* dL_dconic_opacity, /* [n,4] */
+                            const float* dL_dviewspace_out, /* [n,4] */
+                            const int32_t* radii, const uint8_t* clamped,
+                            float* dL_dmeans3d, float* dL_ddc, float* dL_dsh,
+                            float* dL_dcolors_precomp, float* dL_dopacities, float* dL_dscales,
+                            float* dL_dquats, float* dL_dviewspace_in, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FASTGS_B200_H */
