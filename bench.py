@@ -1,0 +1,316 @@
+"""Benchmark: FastGS training step at 1M Gaussians, 1920x1080, SH degree 3.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one view per GPU (weak scaling over the view batch): preprocess ->
+scan -> duplicate -> onesweep sort -> tile prep -> rasterize forward -> L1 +
+0.2 D-SSIM loss -> rasterize backward -> preprocess backward (+ activations,
+densification statistics) -> [NCCL all-reduce of the 59 gradient floats and
+3 statistics per Gaussian, max of screen radii] -> Adam over all parameters.
+Workload: BASELINE config 3 (seeded synthetic scene: 64-component mixture,
+seeded random target images, cameras on a radius-6 orbit). N > 1 runs under
+torchrun, one rank per GPU, NCCL; timings are the max over ranks.
+
+Printed JSON (rank 0): value = views/s of the whole job with parameters,
+targets and state resident in HBM; e2e = the same step through the public API
+with the target image copied from pinned host memory and the loss read back
+each step; roofline of the rasterize-backward kernel (the dominant kernel)
+timed live with CUDA events; cpu_baseline = the same step on the host cores
+(C oracle + numpy, OpenMP over all cores) for one view.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "train iters/s (fwd+bwd) and MPix/s at 1M Gaussians 1080p; 1/2/4/8 GPU"
+WORKLOAD = "config3: 1M Gaussians, 1920x1080, SH degree 3, fwd+bwd+L1/D-SSIM+Adam"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _profile_traffic(name: str):
+    """dram bytes per launch from a committed ncu summary line
+    ``dram_bytes_per_launch: <int>`` in profiles/<name>.md (None if absent)."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    for ln in open(p):
+        if ln.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(float(ln.split(":", 1)[1].strip().split()[0]))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(steps: int = 1):
+    """The same step (one view) on the host cores through the C oracle."""
+    from fastgs_core_b200 import synthetic as S
+    from oracle.cpu_step import cpu_train_step
+
+    scene, cams = S.config3(0)
+    cam = cams[0]
+    tgt = np.random.default_rng(100).uniform(0, 1, (3, cam.height * cam.width)).astype(np.float32)
+    times = []
+    state = None
+    for _ in range(steps):
+        _, dt, state = cpu_train_step(scene, cam, tgt, state)
+        times.append(dt)
+    t = float(np.mean(times))
+    return {"value": 1.0 / t, "unit": "views/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} full config-3 training step(s) of one view on the host "
+                      f"(C oracle fwd/bwd with OpenMP, numpy/scipy loss and Adam); "
+                      f"{t:.2f} s per view"}
+
+
+def run_reference(args):
+    """The reference's CPU path for this step (its eval_cpu is a zero-fill
+    stub, so: the oracle port of its kernels), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    steps = max(1, min(args.steps, 2))
+    cb = cpu_baseline(steps)
+    line = {"metric": METRIC, "value": cb["value"], "unit": "views/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": 0, "ms_per_step": 1000.0 / cb["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": None,
+                       "parallelism": "cpu", "image": "1920x1080", "gaussians": 1_000_000},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "views/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=1_000_000, help="Gaussians (default: config 3)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from fastgs_core_b200 import synthetic as S
+    from fastgs_core_b200.train import Trainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist.group.WORLD
+    warmup = max(3, args.warmup)
+
+    scene, cams = S.config3(0, n=args.n)
+    n_views = max(8, world)
+    rng = np.random.default_rng(0)
+    cams = S.orbit_cameras(rng, n_views, 6.0, 0.0, 1920, 1080, 65.0)
+    W, H = cams[0].width, cams[0].height
+    P = W * H
+    tr = Trainer(scene, dev, process_group=pg)
+    # seeded random targets, resident (value) and pinned on the host (e2e)
+    trng = np.random.default_rng(1000)
+    host_targets = [torch.from_numpy(trng.uniform(0, 1, (3, P)).astype(np.float32)).pin_memory()
+                    for _ in range(n_views)]
+    dev_targets = [t.to(dev) for t in host_targets]
+    loss_dev = torch.zeros(4, device=dev)
+
+    def batch(step):
+        # view v of the batch goes to rank v % world; the batch rotates over the orbit
+        idx = [(step * world + r) % n_views for r in range(world)]
+        return [cams[i] for i in idx], idx
+
+    def one_step(step, targets_for):
+        bc, idx = batch(step)
+        tg = [None] * len(bc)
+        tg[rank] = targets_for(idx[rank])
+        tr.step(bc, tg, loss_out=loss_dev)
+
+    for s in range(warmup):
+        one_step(s, lambda i: dev_targets[i])
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+
+    # ---------------- value: everything resident in HBM
+    tr.record = {"rasterize_backward", "rasterize_forward"}
+    tr.events.clear()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = tr.launches
+    if pg is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    rendered = []
+    for s in range(args.steps):
+        one_step(warmup + s, lambda i: dev_targets[i])
+        rendered.append(tr.last_rendered)
+    e1.record()
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    launches = (tr.launches - launches0) // args.steps
+    bwd_ms = tr.kernel_ms("rasterize_backward")
+    fwd_ms = tr.kernel_ms("rasterize_forward")
+    tr.record = set()
+    t_max = torch.tensor([ms], device=dev)
+    if pg is not None:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms = float(t_max.item())
+
+    # ---------------- e2e: public API with host buffers every step
+    targ = torch.empty((3, P), device=dev)
+    loss_host = torch.empty(4, pin_memory=True)
+    for s in range(3):
+        one_step(s, lambda i: targ.copy_(host_targets[i], non_blocking=True))
+    torch.cuda.synchronize()
+    if pg is not None:
+        dist.barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for s in range(args.steps):
+        one_step(warmup + s, lambda i: targ.copy_(host_targets[i], non_blocking=True))
+        loss_host.copy_(loss_dev, non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+    t_e = torch.tensor([ms_e2e], device=dev)
+    if pg is not None:
+        dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t_e.item())
+
+    if rank == 0:
+        views = world * args.steps
+        value = views / (ms / 1000.0)
+        e2e = views / (ms_e2e / 1000.0)
+        n = tr.n
+        K = float(np.mean(rendered))
+        peak, peak_kind = _peaks()
+        # rasterize backward algorithmic bytes per launch: 40 B per key
+        # (index + record), 32 B per pixel (cotangent, T_final, n_contrib,
+        # pixel colour, bucket state), 52 B per Gaussian (gradient partials)
+        bwd_bytes = 40 * K + 32 * P + 52 * n
+        achieved = bwd_bytes / (bwd_ms / 1000.0) / 1e9 if bwd_ms else None
+        traffic = _profile_traffic("raster_bwd_config3")
+        line = {
+            "metric": METRIC, "value": value, "unit": "views/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded config-3 scene, random targets)",
+            "config": {"workload": WORKLOAD, "model": "3DGS/FastGS rasterizer", "global_batch": world,
+                       "seq_len": None, "parallelism": f"dp{world} (view-sharded)",
+                       "gaussians": n, "image": f"{W}x{H}", "views_per_gpu_per_step": 1,
+                       "l2": "inputs larger than L2 (params+Adam state 944 MB)",
+                       "mean_keys_per_view": K},
+            "iters_per_s": args.steps / (ms / 1000.0),
+            "mpix_per_s": value * P / 1e6,
+            "gpu_launches": launches,
+            "kernel_ms": {"rasterize_backward": bwd_ms, "rasterize_forward": fwd_ms},
+            "roofline": {"kernel": "rasterize_backward", "bound": "hbm", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
+                         "peak_kind": peak_kind, "algorithmic_bytes": bwd_bytes,
+                         "traffic": traffic},
+            "e2e": {"value": e2e, "unit": "views/s", "h2d_bytes_per_step": world * 3 * P * 4 + 140 * world,
+                    "d2h_bytes_per_step": 16},
+            "clocks": clk,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(1)
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -46,6 +46,16 @@ _SIGS = {
     "fgs_rasterize_forward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 18),
     "fgs_rasterize_backward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 20),
     "fgs_preprocess_backward": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 24),
+    "fgs_activate_params": (C.c_int, [_i64, _p, _p, _p, _p, _p]),
+    "fgs_preprocess_backward_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 16
+                                      + [_i32, _p, _p, _p]),
+    "fgs_loss_scratch_bytes": (_sz, [_i32, _i32]),
+    "fgs_l1_dssim_loss": (C.c_int, [_i32, _i32, _p, _p, _f, _f, _p, _p, _p, _p]),
+    "fgs_adam_step": (C.c_int, [_i64, _p, _p, _p, _p, _i32, C.POINTER(_i64), C.POINTER(_f), _f, _f,
+                                _f, _i32, _i32, _p]),
+    "fgs_metric_map": (C.c_int, [_i64, _p, _p, _f, _p, _p, _p, _p]),
+    "fgs_score_accumulate": (C.c_int, [_i64, _p, _p, _i64, _p, _p, _p]),
+    "fgs_score_finalize": (C.c_int, [_i64, _p, _p, _i32, _p, _p, _p, _p]),
 }
 
 _lib = None

@@ -367,12 +367,19 @@ struct PbwdArgs {
   const int32_t* radii;
   const uint8_t* clamped;
   float *dmeans3d, *ddc, *dsh, *dcolors_precomp, *dopac, *dscales, *dquats, *dvs_in;
+  // training mode (kTrain): gradients w.r.t. the raw parameters, accumulated
+  // into a flat buffer, plus densification statistics
+  const float *opac_act, *quats_raw;
+  float *g_means, *g_dc, *g_rest, *g_logit, *g_logscale, *g_rot;
+  float *st_acc, *st_acc_abs, *st_denom, *st_max_radii;
+  int accumulate;
 };
 
 __device__ __forceinline__ v3 v3s(float s, v3 a) { return V3(s * a.x, s * a.y, s * a.z); }
 __device__ __forceinline__ v3 v3sr(v3 a, float s) { return V3(a.x * s, a.y * s, a.z * s); }
 __device__ __forceinline__ v3 v3add(v3 a, v3 b) { return V3(a.x + b.x, a.y + b.y, a.z + b.z); }
 
+template <bool kTrain>
 __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a) {
   extern __shared__ float s_buf[];  // [2][kPreThreads * S3]: staged sh, then dsh
   const fgs_preprocess_params& P = a.p;
@@ -388,6 +395,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
     for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) s_dsh[k] = 0.0f;
     __syncthreads();
   }
+  int32_t my_radius = 0;
+  float4 my_dvs = make_float4(0.f, 0.f, 0.f, 0.f);
   if (i < P.n) {
     float dm[3] = {0.f, 0.f, 0.f};
     float ddc[3] = {0.f, 0.f, 0.f};
@@ -648,25 +657,76 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
       }
       dvs = reinterpret_cast<const float4*>(a.dvs_out)[i];
     }
+    if constexpr (!kTrain) {
 #pragma unroll
-    for (int c = 0; c < 3; ++c) {
-      a.dmeans3d[3 * (int64_t)i + c] = dm[c];
-      a.ddc[3 * (int64_t)i + c] = ddc[c];
-      a.dcolors_precomp[3 * (int64_t)i + c] = dcp[c];
-      a.dscales[3 * (int64_t)i + c] = dsc[c];
+      for (int c = 0; c < 3; ++c) {
+        a.dmeans3d[3 * (int64_t)i + c] = dm[c];
+        a.ddc[3 * (int64_t)i + c] = ddc[c];
+        a.dcolors_precomp[3 * (int64_t)i + c] = dcp[c];
+        a.dscales[3 * (int64_t)i + c] = dsc[c];
+      }
+      a.dopac[i] = dop;
+      reinterpret_cast<float4*>(a.dquats)[i] = make_float4(dq[0], dq[1], dq[2], dq[3]);
+      reinterpret_cast<float4*>(a.dvs_in)[i] = dvs;
+    } else {
+      // activation backward: opacity = sigmoid(logit), scale = exp(log_scale),
+      // quat = q / (|q| + 1e-8) (the trainers' getters,
+      // scripts/train_scanner_fixed.py:523-535)
+      const float o = a.opac_act[i];
+      const float dlogit = dop * o * (1.0f - o);
+      float dls[3];
+#pragma unroll
+      for (int c = 0; c < 3; ++c) dls[c] = dsc[c] * a.scales[3 * (int64_t)i + c];
+      const float4 qr = reinterpret_cast<const float4*>(a.quats_raw)[i];
+      const float qn = sqrtf(qr.x * qr.x + qr.y * qr.y + qr.z * qr.z + qr.w * qr.w);
+      const float inv = 1.0f / (qn + 1e-8f);
+      const float qdot = qr.x * dq[0] + qr.y * dq[1] + qr.z * dq[2] + qr.w * dq[3];
+      const float corr = qn > 0.0f ? qdot * inv * inv / qn : 0.0f;
+      const float dr[4] = {dq[0] * inv - qr.x * corr, dq[1] * inv - qr.y * corr,
+                           dq[2] * inv - qr.z * corr, dq[3] * inv - qr.w * corr};
+      const bool acc = a.accumulate != 0;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        float* gm = a.g_means + 3 * (int64_t)i + c;
+        float* gd = a.g_dc + 3 * (int64_t)i + c;
+        float* gs = a.g_logscale + 3 * (int64_t)i + c;
+        *gm = acc ? *gm + dm[c] : dm[c];
+        *gd = acc ? *gd + ddc[c] : ddc[c];
+        *gs = acc ? *gs + dls[c] : dls[c];
+      }
+      a.g_logit[i] = acc ? a.g_logit[i] + dlogit : dlogit;
+      float4* gr = reinterpret_cast<float4*>(a.g_rot) + i;
+      float4 r4 = make_float4(dr[0], dr[1], dr[2], dr[3]);
+      if (acc) {
+        const float4 o4 = *gr;
+        r4 = make_float4(o4.x + r4.x, o4.y + r4.y, o4.z + r4.z, o4.w + r4.w);
+      }
+      *gr = r4;
+      my_radius = a.radii[i];
+      my_dvs = dvs;
+      // densification statistics (scripts/train_scanner_fastgs.py:391-405)
+      if (my_radius > 0) {
+        a.st_acc[i] += sqrtf(my_dvs.x * my_dvs.x + my_dvs.y * my_dvs.y);
+        a.st_acc_abs[i] += sqrtf(my_dvs.z * my_dvs.z + my_dvs.w * my_dvs.w);
+        a.st_denom[i] += 1.0f;
+        a.st_max_radii[i] = fmax_t(a.st_max_radii[i], (float)my_radius);
+      }
     }
-    a.dopac[i] = dop;
-    reinterpret_cast<float4*>(a.dquats)[i] = make_float4(dq[0], dq[1], dq[2], dq[3]);
-    reinterpret_cast<float4*>(a.dvs_in)[i] = dvs;
   }
+  float* dsh_dst = kTrain ? a.g_rest : a.dsh;
   if (sh_path) {
     __syncthreads();
-    float* gdst = a.dsh + (int64_t)base * S3;
-    for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) gdst[k] = s_dsh[k];
-  } else if (S3 > 0 && a.dsh) {
-    float* gdst = a.dsh + (int64_t)base * S3;
+    float* gdst = dsh_dst + (int64_t)base * S3;
+    if (kTrain && a.accumulate) {
+      for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) gdst[k] += s_dsh[k];
+    } else {
+      for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) gdst[k] = s_dsh[k];
+    }
+  } else if (S3 > 0 && dsh_dst && !(kTrain && a.accumulate)) {
+    float* gdst = dsh_dst + (int64_t)base * S3;
     for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) gdst[k] = 0.0f;
   }
+  (void)my_radius;
 }
 
 }  // namespace fgs
@@ -773,6 +833,7 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
                     dL_dquats && dL_dviewspace_in && (p->max_sh_coeffs == 0 || dL_dsh),
                 "missing output pointer");
   PbwdArgs a;
+  memset(&a, 0, sizeof(a));
   a.p = *p;
   a.focal_x = 0.5f * (float)p->image_width / (p->tan_fovx < 1e-6f ? 1e-6f : p->tan_fovx);
   a.focal_y = 0.5f * (float)p->image_height / (p->tan_fovy < 1e-6f ? 1e-6f : p->tan_fovy);
@@ -785,10 +846,63 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
   const bool sh_path = !p->use_colors_precomp && p->max_sh_coeffs > 0;
   const size_t smem = sh_path ? 2 * (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
   if (smem > 48 * 1024)
-    cudaFuncSetAttribute(preprocess_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(preprocess_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int blocks = (p->n + kPreThreads - 1) / kPreThreads;
-  preprocess_bwd_kernel<<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  preprocess_bwd_kernel<false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_backward");
+}
+
+int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* means3d,
+                                  const float* scales, const float* quats, const float* quats_raw,
+                                  const float* opacities, const float* viewmatrix,
+                                  const float* projmatrix, const float* cam_pos, const float* sh,
+                                  const float* cov3d_fwd, const float* dL_drgb,
+                                  const float* dL_dxys, const float* dL_dconic_opacity,
+                                  const float* dL_dviewspace, const int32_t* radii,
+                                  const uint8_t* clamped, int32_t accumulate, float* grad_flat,
+                                  float* stats, void* stream) {
+  int st = validate_pre(p);
+  if (st) return st;
+  if (p->n == 0) return FGS_OK;
+  FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
+                "training mode needs the scales+quats and dc+sh paths");
+  FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
+  FGS_CHECK_ARG(means3d && scales && quats && quats_raw && opacities && viewmatrix && projmatrix &&
+                    cam_pos && sh && cov3d_fwd && dL_drgb && dL_dxys && dL_dconic_opacity &&
+                    dL_dviewspace && radii && clamped && grad_flat && stats,
+                "missing pointer");
+  const int64_t n = p->n;
+  PbwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.p = *p;
+  a.focal_x = 0.5f * (float)p->image_width / (p->tan_fovx < 1e-6f ? 1e-6f : p->tan_fovx);
+  a.focal_y = 0.5f * (float)p->image_height / (p->tan_fovy < 1e-6f ? 1e-6f : p->tan_fovy);
+  a.means3d = means3d; a.scales = scales; a.quats = quats; a.vm = viewmatrix; a.pm = projmatrix;
+  a.cam_pos = cam_pos; a.sh = sh; a.cov3d_fwd = cov3d_fwd;
+  a.drgb = dL_drgb; a.dxys = dL_dxys; a.dconic = dL_dconic_opacity; a.dvs_out = dL_dviewspace;
+  a.radii = radii; a.clamped = clamped;
+  a.opac_act = opacities; a.quats_raw = quats_raw;
+  a.g_means = grad_flat;
+  a.g_dc = grad_flat + 3 * n;
+  a.g_rest = grad_flat + 6 * n;
+  a.g_logit = grad_flat + 51 * n;
+  a.g_logscale = grad_flat + 52 * n;
+  a.g_rot = grad_flat + 55 * n;
+  a.st_acc = stats;
+  a.st_acc_abs = stats + n;
+  a.st_denom = stats + 2 * n;
+  a.st_max_radii = stats + 3 * n;
+  a.accumulate = accumulate;
+  const size_t smem = 2 * (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(preprocess_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    attr = true;
+  }
+  const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
+  preprocess_bwd_kernel<true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  return check_launch("preprocess_backward_train");
 }
 
 }  // extern "C"

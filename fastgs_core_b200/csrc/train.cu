@@ -1,0 +1,481 @@
+// Training-step kernels around the rasterizer (sm_100a): parameter
+// activations, the L1 + D-SSIM photometric loss and its gradient, the Adam
+// update over the flat parameter buffer, and the FastGS multi-view score
+// accumulation (metric map, contribution counts, importance / pruning
+// scores).
+//
+// Flat parameter / gradient layout (59 floats per Gaussian, N Gaussians):
+//   [0, 3N) means3d | [3N, 6N) features_dc | [6N, 51N) features_rest (15x3)
+//   [51N, 52N) opacity logits | [52N, 55N) log scales | [55N, 59N) rotations
+// This is the buffer the data-parallel step all-reduces.
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/fastgs_b200.h"
+#include "fgs_common.cuh"
+
+namespace fgs {
+
+// ------------------------------------------------------------ activations
+__global__ void activate_kernel(int64_t n, const float* __restrict__ flat, float* __restrict__ opac,
+                                float* __restrict__ scales, float* __restrict__ quats) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float lg = flat[51 * n + i];
+  opac[i] = 1.0f / (1.0f + expf(-lg));
+#pragma unroll
+  for (int c = 0; c < 3; ++c) scales[3 * i + c] = expf(flat[52 * n + 3 * i + c]);
+  const float4 q = reinterpret_cast<const float4*>(flat + 55 * n)[i];
+  const float inv = 1.0f / (sqrtf(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w) + 1e-8f);
+  reinterpret_cast<float4*>(quats)[i] = make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
+}
+
+// --------------------------------------------------------------- L1 + SSIM
+// 11x11 Gaussian window, sigma 1.5 (separable), zero padding, C1 = 0.01^2,
+// C2 = 0.03^2; loss = w_l1 * mean|x - y| + w_ssim * (1 - mean SSIM(x, y)) over
+// the 3 x H x W image (x = render, y = target, both CHW).
+constexpr int kR = 5;
+constexpr int kT = 16;
+constexpr int kS = kT + 2 * kR;  // 26
+__constant__ float c_win[11];
+
+__global__ void __launch_bounds__(256)
+    ssim_fwd_kernel(int W, int H, const float* __restrict__ x, const float* __restrict__ y,
+                    float* __restrict__ maps, float* __restrict__ partials) {
+  __shared__ float s_x[kS][kS + 1];
+  __shared__ float s_y[kS][kS + 1];
+  __shared__ float s_h[5][kS][kT + 1];
+  __shared__ float s_red[2][8];
+  const int tx0 = blockIdx.x * kT, ty0 = blockIdx.y * kT;
+  const int c = blockIdx.z;
+  const size_t P = (size_t)W * H;
+  const float* xc = x + c * P;
+  const float* yc = y + c * P;
+  const int t = threadIdx.x;
+  for (int k = t; k < kS * kS; k += 256) {
+    const int r = k / kS, q = k % kS;
+    const int gy = ty0 - kR + r, gx = tx0 - kR + q;
+    const bool in = gx >= 0 && gx < W && gy >= 0 && gy < H;
+    s_x[r][q] = in ? xc[(size_t)gy * W + gx] : 0.0f;
+    s_y[r][q] = in ? yc[(size_t)gy * W + gx] : 0.0f;
+  }
+  __syncthreads();
+  for (int k = t; k < kS * kT; k += 256) {
+    const int r = k / kT, q = k % kT;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 11; ++j) {
+      const float w = c_win[j], xv = s_x[r][q + j], yv = s_y[r][q + j];
+      a0 += w * xv;
+      a1 += w * yv;
+      a2 += w * xv * xv;
+      a3 += w * yv * yv;
+      a4 += w * xv * yv;
+    }
+    s_h[0][r][q] = a0;
+    s_h[1][r][q] = a1;
+    s_h[2][r][q] = a2;
+    s_h[3][r][q] = a3;
+    s_h[4][r][q] = a4;
+  }
+  __syncthreads();
+  const int ly = t / kT, lx = t % kT;
+  const int gy = ty0 + ly, gx = tx0 + lx;
+  float mu_x = 0.f, mu_y = 0.f, exx = 0.f, eyy = 0.f, exy = 0.f;
+#pragma unroll
+  for (int j = 0; j < 11; ++j) {
+    const float w = c_win[j];
+    mu_x += w * s_h[0][ly + j][lx];
+    mu_y += w * s_h[1][ly + j][lx];
+    exx += w * s_h[2][ly + j][lx];
+    eyy += w * s_h[3][ly + j][lx];
+    exy += w * s_h[4][ly + j][lx];
+  }
+  float ssim = 0.f, l1 = 0.f;
+  if (gx < W && gy < H) {
+    const float C1 = 0.0001f, C2 = 0.0009f;
+    const float A = 2.f * mu_x * mu_y + C1;
+    const float B = 2.f * (exy - mu_x * mu_y) + C2;
+    const float Cc = mu_x * mu_x + mu_y * mu_y + C1;
+    const float D = (exx - mu_x * mu_x) + (eyy - mu_y * mu_y) + C2;
+    const float inv = 1.0f / (Cc * D);
+    ssim = A * B * inv;
+    const float d_mu = 2.f * mu_y * (B - A) * inv - 2.f * mu_x * ssim * (1.f / Cc - 1.f / D);
+    const float d_exx = -ssim / D;
+    const float d_exy = 2.f * A * inv;
+    const size_t pix = (size_t)gy * W + gx;
+    maps[(0 * 3 + c) * P + pix] = d_mu;
+    maps[(1 * 3 + c) * P + pix] = d_exx;
+    maps[(2 * 3 + c) * P + pix] = d_exy;
+    l1 = fabsf(s_x[ly + kR][lx + kR] - s_y[ly + kR][lx + kR]);
+  }
+  // block partial sums (deterministic per block)
+  float a = ssim, b = l1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if ((t & 31) == 0) {
+    s_red[0][t >> 5] = a;
+    s_red[1][t >> 5] = b;
+  }
+  __syncthreads();
+  if (t == 0) {
+    float sa = 0.f, sb = 0.f;
+    for (int k = 0; k < 8; ++k) {
+      sa += s_red[0][k];
+      sb += s_red[1][k];
+    }
+    const size_t blk = ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    partials[2 * blk] = sa;
+    partials[2 * blk + 1] = sb;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    ssim_bwd_kernel(int W, int H, const float* __restrict__ x, const float* __restrict__ y,
+                    const float* __restrict__ maps, float w_l1_n, float w_ssim_n,
+                    float* __restrict__ dx) {
+  __shared__ float s_m[3][kS][kS + 1];
+  __shared__ float s_h[3][kS][kT + 1];
+  const int tx0 = blockIdx.x * kT, ty0 = blockIdx.y * kT;
+  const int c = blockIdx.z;
+  const size_t P = (size_t)W * H;
+  const int t = threadIdx.x;
+  for (int k = t; k < kS * kS; k += 256) {
+    const int r = k / kS, q = k % kS;
+    const int gy = ty0 - kR + r, gx = tx0 - kR + q;
+    const bool in = gx >= 0 && gx < W && gy >= 0 && gy < H;
+    const size_t pix = (size_t)gy * W + gx;
+#pragma unroll
+    for (int m = 0; m < 3; ++m) s_m[m][r][q] = in ? maps[(m * 3 + c) * P + pix] : 0.0f;
+  }
+  __syncthreads();
+  for (int k = t; k < kS * kT; k += 256) {
+    const int r = k / kT, q = k % kT;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 11; ++j) {
+      const float w = c_win[j];
+      a0 += w * s_m[0][r][q + j];
+      a1 += w * s_m[1][r][q + j];
+      a2 += w * s_m[2][r][q + j];
+    }
+    s_h[0][r][q] = a0;
+    s_h[1][r][q] = a1;
+    s_h[2][r][q] = a2;
+  }
+  __syncthreads();
+  const int ly = t / kT, lx = t % kT;
+  const int gy = ty0 + ly, gx = tx0 + lx;
+  if (gx >= W || gy >= H) return;
+  float g0 = 0.f, g1 = 0.f, g2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 11; ++j) {
+    const float w = c_win[j];
+    g0 += w * s_h[0][ly + j][lx];
+    g1 += w * s_h[1][ly + j][lx];
+    g2 += w * s_h[2][ly + j][lx];
+  }
+  const size_t pix = (size_t)gy * W + gx;
+  const float xv = x[c * P + pix], yv = y[c * P + pix];
+  const float sgn = xv > yv ? 1.f : (xv < yv ? -1.f : 0.f);
+  dx[c * P + pix] = w_l1_n * sgn - w_ssim_n * (g0 + 2.f * xv * g1 + yv * g2);
+}
+
+__global__ void loss_finalize_kernel(const float* __restrict__ partials, int nblk, float w_l1,
+                                     float w_ssim, float inv_n, float* __restrict__ out) {
+  __shared__ float s[2][32];
+  float a = 0.f, b = 0.f;
+  for (int k = threadIdx.x; k < nblk; k += blockDim.x) {
+    a += partials[2 * k];
+    b += partials[2 * k + 1];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s[0][threadIdx.x >> 5] = a;
+    s[1][threadIdx.x >> 5] = b;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float sa = 0.f, sb = 0.f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) {
+      sa += s[0][k];
+      sb += s[1][k];
+    }
+    const float ssim = sa * inv_n, l1 = sb * inv_n;
+    out[0] = w_l1 * l1 + w_ssim * (1.0f - ssim);
+    out[1] = l1;
+    out[2] = ssim;
+  }
+}
+
+// -------------------------------------------------------------------- Adam
+struct AdamGroups {
+  int64_t end[8];
+  float lr[8];
+  int count;
+};
+
+__global__ void adam_kernel(int64_t total, float* __restrict__ p, const float* __restrict__ g,
+                            float* __restrict__ m, float* __restrict__ v, AdamGroups grp, float b1,
+                            float b2, float eps, float bc1, float bc2) {
+  const int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t i = 4 * i4;
+  if (i >= total) return;
+  if (i + 4 <= total) {
+    float4 pp = reinterpret_cast<float4*>(p)[i4];
+    const float4 gg = reinterpret_cast<const float4*>(g)[i4];
+    float4 mm = reinterpret_cast<float4*>(m)[i4];
+    float4 vv = reinterpret_cast<float4*>(v)[i4];
+    float* pa = &pp.x;
+    const float* ga = &gg.x;
+    float* ma = &mm.x;
+    float* va = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t idx = i + k;
+      float lr = grp.lr[grp.count - 1];
+      for (int q = 0; q < grp.count; ++q)
+        if (idx < grp.end[q]) {
+          lr = grp.lr[q];
+          break;
+        }
+      ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
+      va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
+      pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
+    }
+    reinterpret_cast<float4*>(p)[i4] = pp;
+    reinterpret_cast<float4*>(m)[i4] = mm;
+    reinterpret_cast<float4*>(v)[i4] = vv;
+  } else {
+    for (int64_t idx = i; idx < total; ++idx) {
+      float lr = grp.lr[grp.count - 1];
+      for (int q = 0; q < grp.count; ++q)
+        if (idx < grp.end[q]) {
+          lr = grp.lr[q];
+          break;
+        }
+      m[idx] = b1 * m[idx] + (1.f - b1) * g[idx];
+      v[idx] = b2 * v[idx] + (1.f - b2) * g[idx] * g[idx];
+      p[idx] -= lr * (m[idx] * bc1) / (sqrtf(v[idx] * bc2) + eps);
+    }
+  }
+}
+
+// ------------------------------------------------------------ FastGS scores
+// scripts/train_scanner_fastgs.py:262-340
+__global__ void l1_map_kernel(int64_t P, const float* __restrict__ pred,
+                              const float* __restrict__ tgt, float* __restrict__ l1map,
+                              unsigned int* __restrict__ minmax, float* __restrict__ l1sum) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float s = 0.f;
+  if (i < P) {
+    const float a = fabsf(pred[i] - tgt[i]);
+    const float b = fabsf(pred[P + i] - tgt[P + i]);
+    const float c = fabsf(pred[2 * P + i] - tgt[2 * P + i]);
+    s = a + b + c;
+    const float mval = s / 3.0f;
+    l1map[i] = mval;
+    // non-negative floats order like their bit patterns
+    atomicMin(minmax, __float_as_uint(mval));
+    atomicMax(minmax + 1, __float_as_uint(mval));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) atomicAdd(l1sum, s);
+}
+
+__global__ void metric_map_kernel(int64_t P, const float* __restrict__ l1map,
+                                  const unsigned int* __restrict__ minmax, float thresh,
+                                  int32_t* __restrict__ metric_map) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  const float mn = __uint_as_float(minmax[0]), mx = __uint_as_float(minmax[1]);
+  const float denom = fmaxf(mx - mn, 1.0e-6f);
+  metric_map[i] = ((l1map[i] - mn) / denom) > thresh ? 1 : 0;
+}
+
+__global__ void score_accumulate_kernel(int64_t n, const int32_t* __restrict__ counts,
+                                        const float* __restrict__ l1sum, float inv_elems,
+                                        float* __restrict__ counts_acc, float* __restrict__ score_acc) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float c = (float)counts[i];
+  const float photometric = l1sum[0] * inv_elems;
+  counts_acc[i] += c;
+  score_acc[i] += photometric * c;
+}
+
+__global__ void minmax_kernel(int64_t n, const float* __restrict__ x, unsigned int* __restrict__ mm) {
+  // order-preserving map of any float to unsigned
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t b = __float_as_uint(x[i]);
+  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  atomicMin(mm, k);
+  atomicMax(mm + 1, k);
+}
+
+__device__ __forceinline__ float unkey(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__global__ void score_finalize_kernel(int64_t n, const float* __restrict__ counts_acc,
+                                      const float* __restrict__ score_acc,
+                                      const unsigned int* __restrict__ mm, float inv_views,
+                                      float* __restrict__ importance, float* __restrict__ pruning) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float mn = unkey(mm[0]), mx = unkey(mm[1]);
+  if (importance) importance[i] = floorf(counts_acc[i] * inv_views);
+  pruning[i] = (score_acc[i] - mn) / fmaxf(mx - mn, 1.0e-6f);
+}
+
+__global__ void init_pair_kernel(unsigned int* p, unsigned int a, unsigned int b) {
+  p[0] = a;
+  p[1] = b;
+}
+
+static bool g_win_ready[64] = {false};  // per device: c_win lives in each device's constant bank
+static int ensure_window() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && g_win_ready[dev]) return FGS_OK;
+  float w[11];
+  double s = 0.0, e[11];
+  for (int i = 0; i < 11; ++i) {
+    e[i] = exp(-((i - 5) * (i - 5)) / (2.0 * 1.5 * 1.5));
+    s += e[i];
+  }
+  for (int i = 0; i < 11; ++i) w[i] = (float)(e[i] / s);
+  cudaError_t err = cudaMemcpyToSymbol(c_win, w, sizeof(w));
+  if (err != cudaSuccess) {
+    set_error("ssim window upload: %s", cudaGetErrorString(err));
+    return FGS_ERR_CUDA;
+  }
+  if (dev >= 0 && dev < 64) g_win_ready[dev] = true;
+  return FGS_OK;
+}
+
+}  // namespace fgs
+
+using namespace fgs;
+
+extern "C" {
+
+int fgs_activate_params(int64_t n, const float* params_flat, float* opacities, float* scales,
+                        float* quats, void* stream) {
+  FGS_CHECK_ARG(n >= 0, "n must be >= 0");
+  if (n == 0) return FGS_OK;
+  FGS_CHECK_ARG(params_flat && opacities && scales && quats, "missing pointer");
+  activate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      n, params_flat, opacities, scales, quats);
+  return check_launch("activate_params");
+}
+
+size_t fgs_loss_scratch_bytes(int32_t width, int32_t height) {
+  const size_t P = (size_t)width * height;
+  const size_t blocks = (size_t)((width + kT - 1) / kT) * ((height + kT - 1) / kT) * 3;
+  return (9 * P + 2 * blocks) * sizeof(float);
+}
+
+int fgs_l1_dssim_loss(int32_t width, int32_t height, const float* image, const float* target,
+                      float w_l1, float w_ssim, float* loss_out, float* dL_dimage, void* scratch,
+                      void* stream) {
+  FGS_CHECK_ARG(width > 0 && height > 0, "image size must be positive");
+  FGS_CHECK_ARG(image && target && loss_out && dL_dimage && scratch, "missing pointer");
+  int st = ensure_window();
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t P = (size_t)width * height;
+  float* maps = (float*)scratch;
+  float* partials = maps + 9 * P;
+  dim3 grid((width + kT - 1) / kT, (height + kT - 1) / kT, 3);
+  const int nblk = (int)(grid.x * grid.y * grid.z);
+  ssim_fwd_kernel<<<grid, 256, 0, s>>>(width, height, image, target, maps, partials);
+  const float inv_n = 1.0f / (float)(3 * P);
+  loss_finalize_kernel<<<1, 1024, 0, s>>>(partials, nblk, w_l1, w_ssim, inv_n, loss_out);
+  ssim_bwd_kernel<<<grid, 256, 0, s>>>(width, height, image, target, maps, w_l1 * inv_n,
+                                       w_ssim * inv_n, dL_dimage);
+  return check_launch("l1_dssim_loss");
+}
+
+int fgs_adam_step(int64_t total, float* params, const float* grads, float* exp_avg,
+                  float* exp_avg_sq, int32_t num_groups, const int64_t* group_end,
+                  const float* group_lr, float beta1, float beta2, float eps, int32_t step,
+                  int32_t bias_correction, void* stream) {
+  FGS_CHECK_ARG(total >= 0, "total must be >= 0");
+  FGS_CHECK_ARG(num_groups >= 1 && num_groups <= 8, "num_groups must be in [1, 8]");
+  FGS_CHECK_ARG(group_end && group_lr, "missing group table");
+  if (total == 0) return FGS_OK;
+  FGS_CHECK_ARG(params && grads && exp_avg && exp_avg_sq, "missing pointer");
+  FGS_CHECK_ARG(((uintptr_t)params | (uintptr_t)grads | (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq) % 16 == 0,
+                "Adam buffers must be 16-byte aligned");
+  AdamGroups g;
+  memset(&g, 0, sizeof(g));
+  g.count = num_groups;
+  for (int k = 0; k < num_groups; ++k) {
+    g.end[k] = group_end[k];
+    g.lr[k] = group_lr[k];
+  }
+  float bc1 = 1.f, bc2 = 1.f;
+  if (bias_correction) {
+    FGS_CHECK_ARG(step >= 1, "step must be >= 1 with bias correction");
+    bc1 = 1.0f / (1.0f - powf(beta1, (float)step));
+    bc2 = 1.0f / (1.0f - powf(beta2, (float)step));
+  }
+  const int64_t n4 = (total + 3) / 4;
+  adam_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      total, params, grads, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
+  return check_launch("adam_step");
+}
+
+int fgs_metric_map(int64_t num_pixels, const float* pred, const float* target, float loss_thresh,
+                   int32_t* metric_map, float* l1_sum, void* scratch, void* stream) {
+  FGS_CHECK_ARG(num_pixels > 0, "num_pixels must be > 0");
+  FGS_CHECK_ARG(pred && target && metric_map && l1_sum && scratch, "missing pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  float* l1map = (float*)scratch;
+  unsigned int* mm = (unsigned int*)(l1map + num_pixels);
+  init_pair_kernel<<<1, 1, 0, s>>>(mm, 0x7f800000u, 0u);
+  cudaMemsetAsync(l1_sum, 0, sizeof(float), s);
+  const unsigned blocks = (unsigned)((num_pixels + 255) / 256);
+  l1_map_kernel<<<blocks, 256, 0, s>>>(num_pixels, pred, target, l1map, mm, l1_sum);
+  metric_map_kernel<<<blocks, 256, 0, s>>>(num_pixels, l1map, mm, loss_thresh, metric_map);
+  return check_launch("metric_map");
+}
+
+int fgs_score_accumulate(int64_t n, const int32_t* metric_count, const float* l1_sum,
+                         int64_t num_elements, float* counts_acc, float* score_acc, void* stream) {
+  FGS_CHECK_ARG(n >= 0 && num_elements > 0, "bad sizes");
+  if (n == 0) return FGS_OK;
+  FGS_CHECK_ARG(metric_count && l1_sum && counts_acc && score_acc, "missing pointer");
+  score_accumulate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      n, metric_count, l1_sum, 1.0f / (float)num_elements, counts_acc, score_acc);
+  return check_launch("score_accumulate");
+}
+
+int fgs_score_finalize(int64_t n, const float* counts_acc, const float* score_acc, int32_t n_views,
+                       float* importance, float* pruning, void* scratch, void* stream) {
+  FGS_CHECK_ARG(n >= 0, "n must be >= 0");
+  if (n == 0) return FGS_OK;
+  FGS_CHECK_ARG(score_acc && pruning && scratch && (importance == nullptr || counts_acc),
+                "missing pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned int* mm = (unsigned int*)scratch;
+  init_pair_kernel<<<1, 1, 0, s>>>(mm, 0xffffffffu, 0u);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  minmax_kernel<<<blocks, 256, 0, s>>>(n, score_acc, mm);
+  score_finalize_kernel<<<blocks, 256, 0, s>>>(n, counts_acc, score_acc, mm,
+                                               1.0f / (float)(n_views > 0 ? n_views : 1),
+                                               importance, pruning);
+  return check_launch("score_finalize");
+}
+
+}  // extern "C"

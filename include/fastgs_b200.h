@@ -218,6 +218,79 @@ FGS_API int fgs_preprocess_backward(const fgs_preprocess_params* p, const float*
                             float* dL_dcolors_precomp, float* dL_dopacities, float* dL_dscales,
                             float* dL_dquats, float* dL_dviewspace_in, void* stream);
 
+/* ===========================================================================
+ * Training-step entry points (new here: the reference does this work in
+ * Python/MLX inside its training scripts, as cited per function).
+ *
+ * Flat parameter / gradient layout, 59 floats per Gaussian, N Gaussians:
+ *   [0,3N) means3d  [3N,6N) features_dc  [6N,51N) features_rest [N,15,3]
+ *   [51N,52N) opacity logits  [52N,55N) log scales  [55N,59N) rotations (raw)
+ * Densification statistics `stats`, 4N floats: [0,N) sum |grad_xy|,
+ *   [N,2N) sum |grad_abs|, [2N,3N) visible-view count, [3N,4N) max radius.
+ */
+
+/* opacity = sigmoid(logit), scale = exp(log_scale), quat = q / (|q| + 1e-8):
+ * the getters of scripts/train_scanner_fixed.py:523-535. */
+FGS_API int fgs_activate_params(int64_t n, const float* params_flat, float* opacities,
+                                float* scales, float* quats, void* stream);
+
+/* Preprocess backward for training: as fgs_preprocess_backward (scales+quats
+ * and dc+sh paths, 15 SH rest coefficients), chained through the activations
+ * above, written (accumulate == 0) or added (accumulate != 0) into the flat
+ * gradient buffer, and the densification statistics of
+ * scripts/train_scanner_fastgs.py:391-405 updated for Gaussians with
+ * radii > 0 from dL_dviewspace. */
+FGS_API int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* means3d,
+                                          const float* scales, const float* quats,
+                                          const float* quats_raw, const float* opacities,
+                                          const float* viewmatrix, const float* projmatrix,
+                                          const float* cam_pos, const float* sh,
+                                          const float* cov3d_fwd, const float* dL_drgb,
+                                          const float* dL_dxys, const float* dL_dconic_opacity,
+                                          const float* dL_dviewspace, const int32_t* radii,
+                                          const uint8_t* clamped, int32_t accumulate,
+                                          float* grad_flat, float* stats, void* stream);
+
+/* loss = w_l1 * mean|image - target| + w_ssim * (1 - mean SSIM(image, target))
+ * over CHW [3,H,W] float images (SSIM: 11x11 Gaussian window, sigma 1.5, zero
+ * padding, C1 = 0.01^2, C2 = 0.03^2), and dL/dimage. loss_out receives
+ * {loss, mean L1, mean SSIM} (3 floats, device). `scratch` holds
+ * fgs_loss_scratch_bytes(W, H) bytes. The training scripts' loss
+ * (scripts/train_scanner_fastgs.py:949-964) with the D-SSIM term added. */
+FGS_API size_t fgs_loss_scratch_bytes(int32_t width, int32_t height);
+FGS_API int fgs_l1_dssim_loss(int32_t width, int32_t height, const float* image,
+                              const float* target, float w_l1, float w_ssim, float* loss_out,
+                              float* dL_dimage, void* scratch, void* stream);
+
+/* Adam over a flat buffer split into num_groups (<= 8) contiguous groups:
+ * elements [group_end[k-1], group_end[k]) use group_lr[k] (host arrays).
+ * m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2; p -= lr m' / (sqrt(v') + eps),
+ * with m' = m, v' = v unless bias_correction (then / (1 - b^step)): the MLX
+ * optim.Adam the reference trainers use (scripts/train_scanner_fastgs.py:76-99).
+ * Buffers 16-byte aligned. */
+FGS_API int fgs_adam_step(int64_t total, float* params, const float* grads, float* exp_avg,
+                          float* exp_avg_sq, int32_t num_groups, const int64_t* group_end,
+                          const float* group_lr, float beta1, float beta2, float eps, int32_t step,
+                          int32_t bias_correction, void* stream);
+
+/* FastGS multi-view score pass (scripts/train_scanner_fastgs.py:262-340):
+ * fgs_metric_map: per-pixel mean |pred - target| over channels, min-max
+ *   normalised, > loss_thresh -> metric_map [P] int32; *l1_sum (device) gets
+ *   sum |pred - target| over all 3P elements. scratch: 4*P + 8 bytes.
+ * fgs_score_accumulate: counts_acc += metric_count; score_acc +=
+ *   (l1_sum / num_elements) * metric_count.
+ * fgs_score_finalize: importance = floor(counts_acc / n_views) (skipped if
+ *   importance is NULL), pruning = min-max normalised score_acc. scratch: 8 bytes. */
+FGS_API int fgs_metric_map(int64_t num_pixels, const float* pred, const float* target,
+                           float loss_thresh, int32_t* metric_map, float* l1_sum, void* scratch,
+                           void* stream);
+FGS_API int fgs_score_accumulate(int64_t n, const int32_t* metric_count, const float* l1_sum,
+                                 int64_t num_elements, float* counts_acc, float* score_acc,
+                                 void* stream);
+FGS_API int fgs_score_finalize(int64_t n, const float* counts_acc, const float* score_acc,
+                               int32_t n_views, float* importance, float* pruning, void* scratch,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,7 +5,7 @@ import torch
 import fastgs_core_b200 as fg
 
 INT_KEYS = ("radii", "point_offsets", "point_list_keys", "point_list", "ranges", "bucket_count",
-            "bucket_offsets", "n_contrib", "max_contrib")
+            "bucket_offsets")
 GEOM = {"geom_means2d": "xys", "geom_depths": "depths", "geom_cov3d": "cov3d", "geom_rgb": "rgb",
         "geom_conic_opacity": "conic_opacity", "geom_tiles_touched": "tiles_touched",
         "geom_clamped": "clamped", "viewspace_points": "viewspace_points",
