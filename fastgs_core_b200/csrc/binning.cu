@@ -66,15 +66,6 @@ constexpr uint32_t kValueMask = (1u << 30) - 1u;
 constexpr int kSpinLimit = 1 << 22;
 constexpr int kSortDynSmem = kPart * (8 + 4);
 
-struct SortWs {
-  uint32_t* hist;       // [passes][256] global digit counts -> exclusive offsets
-  uint32_t* lookback;   // [passes][parts][256]
-  uint32_t* counters;   // [passes] partition tickets
-  int* err;             // timeout flag
-  uint64_t* tmp_keys;
-  uint32_t* tmp_vals;
-};
-
 __global__ void __launch_bounds__(256)
     sort_histogram_kernel(const uint64_t* __restrict__ keys, int64_t n, int passes,
                           uint32_t* __restrict__ hist) {
@@ -366,11 +357,8 @@ int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_
   const size_t need = fgs_sort_workspace_bytes(num_rendered, key_bits);
   FGS_CHECK_ARG(workspace_bytes >= need, "sort workspace too small: %zu < %zu", workspace_bytes, need);
   const int64_t parts = sort_parts(num_rendered);
-  static bool attr_set = false;  // per process; the attribute is per function, all devices
-  if (!attr_set) {
-    cudaFuncSetAttribute(onesweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSortDynSmem);
-    attr_set = true;
-  }
+  static unsigned long long attr_done = 0;
+  smem_attr_once(onesweep_kernel, kSortDynSmem, &attr_done);
   char* w = (char*)workspace;
   uint32_t* hist = (uint32_t*)w;
   w += align256((size_t)passes * kRadix * 4);

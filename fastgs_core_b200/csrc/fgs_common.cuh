@@ -71,6 +71,38 @@ __device__ __forceinline__ float fgs_logf(float x) {
   return fmaf(fe, 0.693145752f, fmaf(fe, 1.42860677e-06f, ln_m));
 }
 
+// fgs_expf restricted to x in (-87, 0]: same operations and bits (2^k with
+// k in [-126, 0] is applied in one exact multiply instead of two), no range
+// checks. Callers guarantee the domain.
+__device__ __forceinline__ float fgs_expf_neg(float x) {
+  const float k = rintf(__fmul_rn(x, 1.44269502f));
+  float r = fmaf(k, -0.693145752f, x);
+  r = fmaf(k, -1.42860677e-06f, r);
+  float p = 1.98412701e-04f;
+  p = fmaf(p, r, 1.38888892e-03f);
+  p = fmaf(p, r, 8.33333377e-03f);
+  p = fmaf(p, r, 4.16666679e-02f);
+  p = fmaf(p, r, 1.66666672e-01f);
+  p = fmaf(p, r, 5.00000000e-01f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  return __fmul_rn(p, __int_as_float((__float2int_rz(k) + 127) << 23));
+}
+
+// Gaussian exponent of a splat at pixel offset (dx, dy), in the reference's
+// operation order (fastgs_rasterize.metal:106-107), never contracted:
+// -0.5 * (a dx^2 + c dy^2) - b dx dy
+__device__ __forceinline__ float splat_power(float a, float b, float c, float dx, float dy) {
+  const float q = __fadd_rn(__fmul_rn(__fmul_rn(a, dx), dx), __fmul_rn(__fmul_rn(c, dy), dy));
+  return __fsub_rn(__fmul_rn(-0.5f, q), __fmul_rn(__fmul_rn(b, dx), dy));
+}
+
+// Lower bound on the exponent below which a splat of opacity o cannot reach
+// alpha >= 1/255: for o <= 1, o * e^p < e^-5.55 = 0.003887 < 1/255. Skipping
+// those pairs before the exponential gives the same decision as evaluating it.
+// Otherwise -87 (the domain limit of fgs_expf_neg; fgs_expf is 0 below it).
+__device__ __forceinline__ float power_cut(float o) { return o <= 1.0f ? -5.55f : -87.0f; }
+
 __device__ __forceinline__ float fmin_t(float a, float b) { return b < a ? b : a; }
 __device__ __forceinline__ float fmax_t(float a, float b) { return a < b ? b : a; }
 __device__ __forceinline__ int imin(int a, int b) { return b < a ? b : a; }
@@ -131,6 +163,19 @@ constexpr float kSH_C1 = 0.4886025119029199f;
 namespace fgs {
 void set_error(const char* fmt, ...);
 int check_launch(const char* what);
+
+// Raise a kernel's dynamic shared-memory limit once per device (the
+// attribute belongs to the function in each device's context).
+template <typename Kernel>
+inline void smem_attr_once(Kernel* k, int bytes, unsigned long long* done_mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(*done_mask & bit)) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    *done_mask |= bit;
+  }
+}
 }  // namespace fgs
 
 #define FGS_CHECK_ARG(cond, ...)     \

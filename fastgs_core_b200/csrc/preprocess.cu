@@ -780,8 +780,8 @@ int fgs_preprocess_forward(const fgs_preprocess_params* p, const float* means3d,
   a.conic = conic_opacity; a.tiles = tiles_touched; a.clamped = clamped; a.vs_out = viewspace_out;
   const bool use_sh = !p->use_colors_precomp && p->degree > 0 && p->max_sh_coeffs > 0;
   const size_t smem = use_sh ? (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(preprocess_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(preprocess_fwd_kernel, (int)smem, &attr_done);
   const int blocks = (p->n + kPreThreads - 1) / kPreThreads;
   preprocess_fwd_kernel<<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_forward");
@@ -845,8 +845,8 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
   a.dopac = dL_dopacities; a.dscales = dL_dscales; a.dquats = dL_dquats; a.dvs_in = dL_dviewspace_in;
   const bool sh_path = !p->use_colors_precomp && p->max_sh_coeffs > 0;
   const size_t smem = sh_path ? 2 * (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(preprocess_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<false>, (int)smem, &attr_done);
   const int blocks = (p->n + kPreThreads - 1) / kPreThreads;
   preprocess_bwd_kernel<false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_backward");
@@ -894,12 +894,8 @@ int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* m
   a.st_max_radii = stats + 3 * n;
   a.accumulate = accumulate;
   const size_t smem = 2 * (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(preprocess_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<true>, (int)smem, &attr_done);
   const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
   preprocess_bwd_kernel<true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_backward_train");

@@ -24,12 +24,14 @@
  *   - min(a,b) = b<a ? b : a, max(a,b) = a<b ? b : a (the reference's template
  *     reading; NaN selects the first operand);
  *   - float->int conversion truncates toward zero, saturates, NaN -> 0;
- *   - exp/log: with FGS_ORACLE_LIBM they are libm expf/logf (this build is
+ *   - exp/log: with FGS_ORACLE_LIBM they are libm expf/logf and every
+ *     expression keeps the reference's unfused operations (this build is
  *     pinned bit-for-bit against the reference kernels compiled on this CPU);
- *     otherwise they are fgs_expf/fgs_logf below, which the CUDA kernels
- *     implement with the same operations, so integer outputs (tiles touched,
- *     keys, ranges, n_contrib) and the rendered image are bit-identical
- *     between this oracle and the GPU.
+ *     otherwise ("gpu" mode) they are fgs_expf/fgs_logf below and the
+ *     per-splat colour accumulation is one fused multiply-add, exactly as
+ *     the CUDA kernels compute them, so integer outputs (tiles touched, keys,
+ *     ranges, n_contrib) and the rendered image are bit-identical between
+ *     this oracle and the GPU.
  *
  * Defined behaviour where the reference's is undefined:
  *   - max_contrib is the max of n_contrib over in-image pixels of the tile
@@ -113,9 +115,13 @@ static inline float fgs_logf(float x) {
 #ifdef FGS_ORACLE_LIBM
 #define O_EXP(x) expf(x)
 #define O_LOG(x) logf(x)
+/* colour accumulation c += (col * alpha) * T as two rounded ops */
+#define O_ACC(c, ca, t) ((c) + (ca) * (t))
 #else
 #define O_EXP(x) fgs_expf(x)
 #define O_LOG(x) fgs_logf(x)
+/* the CUDA kernels fuse the colour accumulation: c = fma(col * alpha, T, c) */
+#define O_ACC(c, ca, t) fmaf((ca), (t), (c))
 #endif
 
 static inline float fmin_t(float a, float b) { return b < a ? b : a; }
@@ -624,7 +630,7 @@ void o_render_forward(int W, int H, int get_flag, const uint32_t* ranges,
           if (alpha < 1.0f / 255.0f) continue;
           const float test_t = T * (1.0f - alpha);
           if (test_t < 0.0001f) break;
-          for (int ch = 0; ch < 3; ++ch) C[ch] += colors[3 * (size_t)g + ch] * alpha * T;
+          for (int ch = 0; ch < 3; ++ch) C[ch] = O_ACC(C[ch], colors[3 * (size_t)g + ch] * alpha, T);
           if (get_flag && metric_map[pix] == 1) {
 #pragma omp atomic
             metric_count[g] += 1;
