@@ -1,26 +1,30 @@
 // Tile rasterizer backward on sm_100a (fastgs_core/metal/fastgs_rasterize_backward.metal:24-278).
 //
-// One warp per bucket (32 consecutive splats of one tile, one splat per
-// lane). Pixel i of the tile enters at lane 0 on step i with the bucket's
-// sample (transmittance T and the colour accumulated before the bucket) and
-// moves one lane per step, so every pixel is undone through the bucket's 32
-// splats front to back; each lane keeps its splat's gradient partials in
-// registers and adds them with one atomic per output element at the end.
-// Only the mutable blend state (T and the three remaining-colour sums) moves
-// between lanes; the per-pixel read-only data (dL/dpixel, T_final * bg.dL,
-// n_contrib) and the bucket samples are staged once per warp in shared memory.
+// Same gradients as the reference's per-bucket kernel, organised pixel-
+// parallel: one CTA per 16x16 tile, one thread per pixel. The CTA walks the
+// tile's buckets (32 consecutive splats); each pixel starts a bucket from its
+// forward sample (transmittance T and the colour accumulated before the
+// bucket) and undoes the bucket's splats front to back. Per splat, a warp
+// (two pixel rows) skips the splat outright when the splat's opacity-aware
+// row extent misses its rows, or when no lane's pair passes the alpha test
+// (ballot); otherwise the eleven per-pair partials are summed across the warp
+// with a four-level transposed butterfly (lane 2k ends with value k) and added
+// to the bucket's shared-memory accumulators; after the bucket, one global
+// atomic per splat and output element. Compared with one warp per bucket
+// (the reference's layout), this evaluates the same pairs but skips whole
+// warp-splat blocks that cannot contribute and avoids the 31-step pipeline
+// fill of the lane-to-lane state shift.
 //
-// This file is compiled with multiply-add contraction: gradient arithmetic is
-// free to fuse. The per-pair decisions must match the forward pass exactly,
-// so the exponent (splat_power), the opacity product and the exponential use
-// explicitly rounded operations (see fgs_common.cuh).
+// Compiled with multiply-add contraction: gradient arithmetic may fuse. The
+// per-pair decisions must match the forward pass exactly, so the exponent
+// (splat_power), the opacity product and the exponential use explicitly
+// rounded operations (fgs_common.cuh).
 #include "../../include/fastgs_b200.h"
 #include "fgs_common.cuh"
 
 namespace fgs {
 
 constexpr int kTilePx = 256;
-constexpr int kBwdWarps = 8;
 
 struct BwdArgs {
   int W, H, gx, num_tiles;
@@ -46,143 +50,210 @@ struct BwdArgs {
   float* dviewspace;
 };
 
-struct WarpStage {
-  float4 state[kTilePx];  // bucket sample: T, ar0, ar1, ar2 (ar = sampled colour - final colour)
-  float4 ro[kTilePx];     // dL/dpix r, g, b and T_final * (bg . dL/dpix)
-  int last[kTilePx];      // n_contrib (0 outside the image)
-};
+// accumulator slots per splat
+enum { kMx, kMy, kMxAbs, kMyAbs, kCx, kCy, kCw, kOp, kR, kG, kB, kSlots };
 
-__global__ void __launch_bounds__(kBwdWarps * 32) raster_bwd_kernel(BwdArgs a) {
-  extern __shared__ __align__(16) unsigned char s_raw[];
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  WarpStage& S = reinterpret_cast<WarpStage*>(s_raw)[w];
-  const int64_t bucket = (int64_t)blockIdx.x * kBwdWarps + w;
-  if (bucket >= a.bucket_sum) return;
-  const uint32_t tile = a.bucket_to_tile[bucket];
-  if (tile >= (uint32_t)a.num_tiles) return;
+// Conservative tile-local pixel rows [lo, hi] where a splat can reach alpha >=
+// 1/255 (same bound as the forward kernel's row culling).
+__device__ __forceinline__ void bwd_splat_rows(float y, float a, float b, float c, float o, int pminy,
+                                               int& lo, int& hi) {
+  lo = 0;
+  hi = FGS_BLOCK - 1;
+  const float det = a * c - b * b;
+  if (!(a > 0.0f && det > 0.0f && o == o)) return;
+  if (!(o * 255.0f > 1.0f)) {
+    lo = 1;
+    hi = 0;
+    return;
+  }
+  const float L = logf(255.0f * o);
+  const float dymax = sqrtf(2.0f * L * a / det) * 1.001f + 0.01f;
+  if (!(dymax < 1e6f)) return;
+  const float yl = y - (float)pminy;
+  lo = max(-1, (int)ceilf(yl - dymax));
+  hi = min(FGS_BLOCK, (int)floorf(yl + dymax));
+}
+
+// Sum p[0..15] across the warp so that lanes 2k and 2k+1 hold sum_k.
+__device__ __forceinline__ float warp_transpose_sum16(float (&p)[16], int lane) {
+  {
+    const bool hi = lane & 16;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float send = hi ? p[k] : p[k + 8];
+      const float keep = hi ? p[k + 8] : p[k];
+      p[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float send = hi ? p[k] : p[k + 4];
+      const float keep = hi ? p[k + 4] : p[k];
+      p[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float send = hi ? p[k] : p[k + 2];
+      const float keep = hi ? p[k + 2] : p[k];
+      p[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? p[0] : p[1];
+    const float keep = hi ? p[1] : p[0];
+    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
+}
+
+__global__ void __launch_bounds__(kTilePx) raster_bwd_kernel(BwdArgs a) {
+  __shared__ float4 s_r0[32];  // x, y, conic.x, conic.y
+  __shared__ float4 s_r1[32];  // conic.z, opacity, r, g
+  __shared__ float4 s_r2[32];  // b, exponent cut, rows lo / hi (int bits)
+  __shared__ uint32_t s_id[32];
+  __shared__ float s_acc[32][kSlots + 1];
+
+  const int tile = blockIdx.x;
+  const int lr = threadIdx.x, lane = lr & 31;
+  const int wrow = (lr >> 5) * 2;
   const uint2 range = a.ranges[tile];
   const int nsplat = (int)(range.y - range.x);
-  const uint32_t bbm = (tile == 0u) ? 0u : a.bucket_offsets[tile - 1u];
-  const int bidx = (int)((uint32_t)bucket - bbm);
-  if (bidx * 32 >= (int)a.max_contrib[tile]) return;
-
-  const int tx = (int)tile % a.gx, ty = (int)tile / a.gx;
+  const int nb = (nsplat + 31) / 32;
+  const int nb_active = min(nb, (int)((a.max_contrib[tile] + 31u) / 32u));
+  if (nb_active == 0) return;
+  const uint32_t bbm0 = (tile == 0) ? 0u : a.bucket_offsets[tile - 1];
+  const int tx = tile % a.gx, ty = tile / a.gx;
   const int pminx = tx * FGS_BLOCK, pminy = ty * FGS_BLOCK;
+  const int px = pminx + (lr & 15), py = pminy + (lr >> 4);
+  const bool inside = px < a.W && py < a.H;
   const size_t P = (size_t)a.W * a.H;
-  const float bg0 = a.bg[0], bg1 = a.bg[1], bg2 = a.bg[2];
-  // stage this bucket's pixel data: lane takes pixels lane, lane + 32, ...
-  {
-    const float* st = a.sampled_t + (size_t)bucket * kTilePx;
-    const float* sar = a.sampled_ar + (size_t)bucket * 3 * kTilePx;
-    for (int li = lane; li < kTilePx; li += 32) {
-      const int ppx = pminx + (li & 15), ppy = pminy + (li >> 4);
-      if (ppx < a.W && ppy < a.H) {
-        const size_t id = (size_t)ppy * a.W + ppx;
-        const float d0 = a.dL_dout[id], d1 = a.dL_dout[P + id], d2 = a.dL_dout[2 * P + id];
-        const float bg_dot = bg0 * d0 + bg1 * d1 + bg2 * d2;
-        S.state[li] = make_float4(st[li], -a.pixel_colors[id] + sar[li],
-                                  -a.pixel_colors[P + id] + sar[kTilePx + li],
-                                  -a.pixel_colors[2 * P + id] + sar[2 * kTilePx + li]);
-        S.ro[li] = make_float4(d0, d1, d2, a.final_t[id] * bg_dot);
-        S.last[li] = (int)a.n_contrib[id];
-      } else {
-        S.state[li] = make_float4(0.f, 0.f, 0.f, 0.f);
-        S.ro[li] = make_float4(0.f, 0.f, 0.f, 0.f);
-        S.last[li] = 0;
-      }
-    }
+  const size_t pix = inside ? (size_t)py * a.W + px : 0;
+  const float pfx = (float)px, pfy = (float)py;
+  float d0 = 0.f, d1 = 0.f, d2 = 0.f, tfbg = 0.f, pc0 = 0.f, pc1 = 0.f, pc2 = 0.f;
+  int last = 0;
+  if (inside) {
+    d0 = a.dL_dout[pix];
+    d1 = a.dL_dout[P + pix];
+    d2 = a.dL_dout[2 * P + pix];
+    tfbg = a.final_t[pix] * (a.bg[0] * d0 + a.bg[1] * d1 + a.bg[2] * d2);
+    pc0 = a.pixel_colors[pix];
+    pc1 = a.pixel_colors[P + pix];
+    pc2 = a.pixel_colors[2 * P + pix];
+    last = (int)a.n_contrib[pix];
   }
-  __syncwarp();
-
-  const int sidx0 = bidx * 32 + lane;
-  const bool valid_splat = sidx0 < nsplat;
-  const int sidx = valid_splat ? sidx0 : 0x7fffffff;  // never below n_contrib
-  uint32_t g = 0;
-  float2 xy = make_float2(0.f, 0.f);
-  float4 co = make_float4(0.f, 0.f, 0.f, 0.f);
-  float c0 = 0.f, c1 = 0.f, c2 = 0.f;
-  if (valid_splat) {
-    g = a.point_list[range.x + sidx0];
-    xy = a.means2d[g];
-    co = a.conic[g];
-    c0 = a.colors[3 * (size_t)g];
-    c1 = a.colors[3 * (size_t)g + 1];
-    c2 = a.colors[3 * (size_t)g + 2];
-  }
-  const float pcut = power_cut(co.w);
   const float hw = 0.5f * (float)a.W, hh = 0.5f * (float)a.H;
-  float rm_x = 0.f, rm_y = 0.f, rm_z = 0.f, rm_w = 0.f;
-  float rc_x = 0.f, rc_y = 0.f, rc_w = 0.f, rop = 0.f;
-  float rcol0 = 0.f, rcol1 = 0.f, rcol2 = 0.f;
 
-  float T = 0.f, ar0 = 0.f, ar1 = 0.f, ar2 = 0.f;
-  for (int i = 0; i < kTilePx + 31; ++i) {
-    T = __shfl_up_sync(0xffffffffu, T, 1);
-    ar0 = __shfl_up_sync(0xffffffffu, ar0, 1);
-    ar1 = __shfl_up_sync(0xffffffffu, ar1, 1);
-    ar2 = __shfl_up_sync(0xffffffffu, ar2, 1);
-    {
-      const float4 inj = S.state[i & (kTilePx - 1)];
-      if (lane == 0) {
-        T = inj.x;
-        ar0 = inj.y;
-        ar1 = inj.z;
-        ar2 = inj.w;
+  for (int b = 0; b < nb_active; ++b) {
+    const size_t bucket = (size_t)bbm0 + b;
+    __syncthreads();  // previous bucket's accumulators flushed, records free
+    if (lr < 32) {
+      const int s = b * 32 + lr;
+      if (s < nsplat) {
+        const uint32_t g = a.point_list[range.x + s];
+        const float2 xy = a.means2d[g];
+        const float4 co = a.conic[g];
+        int rlo, rhi;
+        bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, pminy, rlo, rhi);
+        s_r0[lr] = make_float4(xy.x, xy.y, co.x, co.y);
+        s_r1[lr] = make_float4(co.z, co.w, a.colors[3 * (size_t)g], a.colors[3 * (size_t)g + 1]);
+        s_r2[lr] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), __int_as_float(rlo),
+                               __int_as_float(rhi));
+        s_id[lr] = g;
+      } else {
+        s_r2[lr] = make_float4(0.f, 0.f, __int_as_float(1), __int_as_float(0));  // no rows
+        s_id[lr] = 0xffffffffu;
       }
     }
-    const int idx = i - lane;
-    if ((unsigned)idx >= (unsigned)kTilePx) continue;
-    if (sidx >= S.last[idx]) continue;
-    const float dx = xy.x - (float)(pminx + (idx & 15));
-    const float dy = xy.y - (float)(pminy + (idx >> 4));
-    const float power = splat_power(co.x, co.y, co.z, dx, dy);
-    if (power > 0.0f || power <= pcut) continue;
-    const float G = fgs_expf_neg(power);
-    const float oG = __fmul_rn(co.w, G);
-    const float alpha = fmin_t(0.99f, oG);
-    if (alpha < 1.0f / 255.0f) continue;
-    const float4 ro = S.ro[idx];
-    const float wgt = alpha * T;
-    const float rec = __fdividef(1.0f, 1.0f - alpha);
-    ar0 += wgt * c0;
-    ar1 += wgt * c1;
-    ar2 += wgt * c2;
-    rcol0 += wgt * ro.x;
-    rcol1 += wgt * ro.y;
-    rcol2 += wgt * ro.z;
-    const float cdot = c0 * ro.x + c1 * ro.y + c2 * ro.z;
-    const float adot = ar0 * ro.x + ar1 * ro.y + ar2 * ro.z;
-    const float dL_dalpha = T * cdot + rec * (adot - ro.w);
-    T *= (1.0f - alpha);
-    if (oG > 0.99f) continue;
-    const float dL_dG = co.w * dL_dalpha;
-    const float gdx = G * dx, gdy = G * dy;
-    const float tmp_x = dL_dG * (-gdx * co.x - gdy * co.y) * hw;
-    const float tmp_y = dL_dG * (-gdy * co.z - gdx * co.y) * hh;
-    rm_x += tmp_x;
-    rm_y += tmp_y;
-    rm_z += fabsf(tmp_x);
-    rm_w += fabsf(tmp_y);
-    const float q = -0.5f * dL_dG;
-    rc_x += q * gdx * dx;
-    rc_y += q * gdx * dy;
-    rc_w += q * gdy * dy;
-    rop += G * dL_dalpha;
-  }
-  if (valid_splat) {
-    atomicAdd(a.dmeans2d + 2 * (size_t)g, rm_x);
-    atomicAdd(a.dmeans2d + 2 * (size_t)g + 1, rm_y);
-    atomicAdd(a.dviewspace + 4 * (size_t)g, rm_x);
-    atomicAdd(a.dviewspace + 4 * (size_t)g + 1, rm_y);
-    atomicAdd(a.dviewspace + 4 * (size_t)g + 2, rm_z);
-    atomicAdd(a.dviewspace + 4 * (size_t)g + 3, rm_w);
-    atomicAdd(a.dconic + 4 * (size_t)g, rc_x);
-    atomicAdd(a.dconic + 4 * (size_t)g + 1, rc_y);
-    atomicAdd(a.dconic + 4 * (size_t)g + 2, rc_w);
-    atomicAdd(a.dconic + 4 * (size_t)g + 3, rop);
-    atomicAdd(a.dcolors + 3 * (size_t)g, rcol0);
-    atomicAdd(a.dcolors + 3 * (size_t)g + 1, rcol1);
-    atomicAdd(a.dcolors + 3 * (size_t)g + 2, rcol2);
+    for (int k = lr; k < 32 * (kSlots + 1); k += kTilePx) (&s_acc[0][0])[k] = 0.0f;
+    float T = a.sampled_t[bucket * kTilePx + lr];
+    const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lr;
+    float ar0 = sar[0] - pc0, ar1 = sar[kTilePx] - pc1, ar2 = sar[2 * kTilePx] - pc2;
+    __syncthreads();
+    const int s0 = b * 32;
+    for (int j = 0; j < 32; ++j) {
+      const float4 r2 = s_r2[j];
+      if (__float_as_int(r2.w) < wrow || __float_as_int(r2.z) > wrow + 1) continue;  // warp-uniform
+      const float4 r0 = s_r0[j];
+      const float4 r1 = s_r1[j];
+      const float dx = r0.x - pfx, dy = r0.y - pfy;
+      const float power = splat_power(r0.z, r0.w, r1.x, dx, dy);
+      // same decisions as the forward pass (NaN exponents included)
+      bool v = (s0 + j < last) && !(power > 0.0f) && !(power <= r2.y);
+      float G = 0.f, oG = 0.f, alpha = 0.f;
+      if (v) {
+        G = fgs_expf_neg(power);
+        oG = __fmul_rn(r1.y, G);
+        alpha = fmin_t(0.99f, oG);
+        v = alpha >= 1.0f / 255.0f;
+      }
+      if (__ballot_sync(0xffffffffu, v) == 0u) continue;  // warp-uniform
+      float p[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) p[k] = 0.0f;
+      if (v) {
+        const float c0 = r1.z, c1 = r1.w, c2 = r2.x;
+        const float wgt = alpha * T;
+        const float rec = __fdividef(1.0f, 1.0f - alpha);
+        ar0 += wgt * c0;
+        ar1 += wgt * c1;
+        ar2 += wgt * c2;
+        p[kR] = wgt * d0;
+        p[kG] = wgt * d1;
+        p[kB] = wgt * d2;
+        const float cdot = c0 * d0 + c1 * d1 + c2 * d2;
+        const float adot = ar0 * d0 + ar1 * d1 + ar2 * d2;
+        const float dL_dalpha = T * cdot + rec * (adot - tfbg);
+        T *= (1.0f - alpha);
+        if (!(oG > 0.99f)) {
+          const float dL_dG = r1.y * dL_dalpha;
+          const float gdx = G * dx, gdy = G * dy;
+          const float tmp_x = dL_dG * (-gdx * r0.z - gdy * r0.w) * hw;
+          const float tmp_y = dL_dG * (-gdy * r1.x - gdx * r0.w) * hh;
+          p[kMx] = tmp_x;
+          p[kMy] = tmp_y;
+          p[kMxAbs] = fabsf(tmp_x);
+          p[kMyAbs] = fabsf(tmp_y);
+          const float q = -0.5f * dL_dG;
+          p[kCx] = q * gdx * dx;
+          p[kCy] = q * gdx * dy;
+          p[kCw] = q * gdy * dy;
+          p[kOp] = G * dL_dalpha;
+        }
+      }
+      const float tot = warp_transpose_sum16(p, lane);
+      const int slot = lane >> 1;
+      if (!(lane & 1) && slot < kSlots) atomicAdd(&s_acc[j][slot], tot);
+    }
+    __syncthreads();
+    for (int k = lr; k < 32 * kSlots; k += kTilePx) {
+      const int j = k / kSlots, slot = k % kSlots;
+      const uint32_t g = s_id[j];
+      if (g == 0xffffffffu) continue;
+      const float v = s_acc[j][slot];
+      float* dst;
+      switch (slot) {
+        case kMx: dst = a.dmeans2d + 2 * (size_t)g; break;
+        case kMy: dst = a.dmeans2d + 2 * (size_t)g + 1; break;
+        case kMxAbs: dst = a.dviewspace + 4 * (size_t)g + 2; break;
+        case kMyAbs: dst = a.dviewspace + 4 * (size_t)g + 3; break;
+        case kCx: dst = a.dconic + 4 * (size_t)g; break;
+        case kCy: dst = a.dconic + 4 * (size_t)g + 1; break;
+        case kCw: dst = a.dconic + 4 * (size_t)g + 2; break;
+        case kOp: dst = a.dconic + 4 * (size_t)g + 3; break;
+        case kR: dst = a.dcolors + 3 * (size_t)g; break;
+        case kG: dst = a.dcolors + 3 * (size_t)g + 1; break;
+        default: dst = a.dcolors + 3 * (size_t)g + 2; break;
+      }
+      atomicAdd(dst, v);
+      if (slot == kMx) atomicAdd(a.dviewspace + 4 * (size_t)g, v);
+      if (slot == kMy) atomicAdd(a.dviewspace + 4 * (size_t)g + 1, v);
+    }
   }
 }
 
@@ -238,11 +309,7 @@ int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
   a.dcolors = dL_dcolors;
   a.dconic = dL_dconic_opacity;
   a.dviewspace = dL_dviewspace;
-  const int smem = (int)(kBwdWarps * sizeof(WarpStage));
-  static unsigned long long attr_done = 0;
-  smem_attr_once(raster_bwd_kernel, smem, &attr_done);
-  const int64_t blocks = (p->bucket_sum + kBwdWarps - 1) / kBwdWarps;
-  raster_bwd_kernel<<<(unsigned)blocks, kBwdWarps * 32, smem, s>>>(a);
+  raster_bwd_kernel<<<p->num_tiles, kTilePx, 0, s>>>(a);
   return check_launch("rasterize_backward");
 }
 
