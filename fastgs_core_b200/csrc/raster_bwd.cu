@@ -1,16 +1,17 @@
 // Tile rasterizer backward on sm_100a (fastgs_core/metal/fastgs_rasterize_backward.metal:24-278).
 //
 // Same gradients as the reference's per-bucket kernel, organised pixel-
-// parallel: one CTA per 16x16 tile, one thread per pixel. The CTA walks the
-// tile's buckets (32 consecutive splats); each pixel starts a bucket from its
-// forward sample (transmittance T and the colour accumulated before the
-// bucket) and undoes the bucket's splats front to back. Per splat, a warp
-// (two pixel rows) skips the splat outright when the splat's opacity-aware
-// row extent misses its rows, or when no lane's pair passes the alpha test
-// (ballot); otherwise the eleven per-pair partials are summed across the warp
-// with a four-level transposed butterfly (lane 2k ends with value k) and added
-// to the bucket's shared-memory accumulators; after the bucket, one global
-// atomic per splat and output element. Compared with one warp per bucket
+// parallel: one CTA per 16x16 tile, one thread per pixel. The CTA stages the
+// records of up to 256 splats (8 buckets) at a time; each warp (two pixel
+// rows) then walks them front to back on its own, restarting each bucket from
+// the pixel's forward sample (transmittance T and the colour accumulated
+// before the bucket, kept as its dot product with dL/dpixel, which is all the
+// alpha gradient needs). Per splat, a warp skips the splat outright when the
+// splat's opacity-aware row extent misses its rows, or when no lane's pair
+// passes the alpha test (ballot); otherwise the eleven per-pair partials are
+// summed across the warp with a five-level transposed butterfly (lane 2k ends
+// with value k) and added to shared-memory accumulators; after the chunk, one
+// global atomic per splat and output element. Compared with one warp per bucket
 // (the reference's layout), this evaluates the same pairs but skips whole
 // warp-splat blocks that cannot contribute and avoids the 31-step pipeline
 // fill of the lane-to-lane state shift.
@@ -112,21 +113,25 @@ __device__ __forceinline__ float warp_transpose_sum16(float (&p)[16], int lane) 
   return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
 }
 
+constexpr int kChunk = 256;  // splats (8 buckets) staged per CTA pass
+
 __global__ void __launch_bounds__(kTilePx) raster_bwd_kernel(BwdArgs a) {
-  __shared__ float4 s_r0[32];  // x, y, conic.x, conic.y
-  __shared__ float4 s_r1[32];  // conic.z, opacity, r, g
-  __shared__ float4 s_r2[32];  // b, exponent cut, rows lo / hi (int bits)
-  __shared__ uint32_t s_id[32];
-  __shared__ float s_acc[32][kSlots + 1];
+  // splat records of the current chunk
+  __shared__ float4 s_r0[kChunk];  // x, y, conic.a, conic.b
+  __shared__ float4 s_r1[kChunk];  // conic.c, opacity, r, g
+  __shared__ float4 s_r2[kChunk];  // b, exponent cut, rows lo / hi (int bits)
+  __shared__ uint32_t s_id[kChunk];
+  __shared__ float s_acc[kChunk][kSlots];
 
   const int tile = blockIdx.x;
   const int lr = threadIdx.x, lane = lr & 31;
   const int wrow = (lr >> 5) * 2;
   const uint2 range = a.ranges[tile];
   const int nsplat = (int)(range.y - range.x);
-  const int nb = (nsplat + 31) / 32;
-  const int nb_active = min(nb, (int)((a.max_contrib[tile] + 31u) / 32u));
-  if (nb_active == 0) return;
+  // buckets at or past max_contrib have no contributing pixel (reference:
+  // fastgs_rasterize_backward.metal:72-74)
+  const int nact = min(nsplat, (int)((a.max_contrib[tile] + 31u) / 32u) * 32);
+  if (nact <= 0) return;
   const uint32_t bbm0 = (tile == 0) ? 0u : a.bucket_offsets[tile - 1];
   const int tx = tile % a.gx, ty = tile / a.gx;
   const int pminx = tx * FGS_BLOCK, pminy = ty * FGS_BLOCK;
@@ -135,48 +140,47 @@ __global__ void __launch_bounds__(kTilePx) raster_bwd_kernel(BwdArgs a) {
   const size_t P = (size_t)a.W * a.H;
   const size_t pix = inside ? (size_t)py * a.W + px : 0;
   const float pfx = (float)px, pfy = (float)py;
-  float d0 = 0.f, d1 = 0.f, d2 = 0.f, tfbg = 0.f, pc0 = 0.f, pc1 = 0.f, pc2 = 0.f;
+  float d0 = 0.f, d1 = 0.f, d2 = 0.f, tfbg = 0.f, pcd = 0.f;
   int last = 0;
   if (inside) {
     d0 = a.dL_dout[pix];
     d1 = a.dL_dout[P + pix];
     d2 = a.dL_dout[2 * P + pix];
     tfbg = a.final_t[pix] * (a.bg[0] * d0 + a.bg[1] * d1 + a.bg[2] * d2);
-    pc0 = a.pixel_colors[pix];
-    pc1 = a.pixel_colors[P + pix];
-    pc2 = a.pixel_colors[2 * P + pix];
+    // final colour . dL/dpix: the per-bucket remaining-colour dot starts from
+    // (sampled colour - final colour) . dL/dpix
+    pcd = a.pixel_colors[pix] * d0 + a.pixel_colors[P + pix] * d1 + a.pixel_colors[2 * P + pix] * d2;
     last = (int)a.n_contrib[pix];
   }
   const float hw = 0.5f * (float)a.W, hh = 0.5f * (float)a.H;
 
-  for (int b = 0; b < nb_active; ++b) {
-    const size_t bucket = (size_t)bbm0 + b;
-    __syncthreads();  // previous bucket's accumulators flushed, records free
-    if (lr < 32) {
-      const int s = b * 32 + lr;
-      if (s < nsplat) {
-        const uint32_t g = a.point_list[range.x + s];
-        const float2 xy = a.means2d[g];
-        const float4 co = a.conic[g];
-        int rlo, rhi;
-        bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, pminy, rlo, rhi);
-        s_r0[lr] = make_float4(xy.x, xy.y, co.x, co.y);
-        s_r1[lr] = make_float4(co.z, co.w, a.colors[3 * (size_t)g], a.colors[3 * (size_t)g + 1]);
-        s_r2[lr] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), __int_as_float(rlo),
-                               __int_as_float(rhi));
-        s_id[lr] = g;
-      } else {
-        s_r2[lr] = make_float4(0.f, 0.f, __int_as_float(1), __int_as_float(0));  // no rows
-        s_id[lr] = 0xffffffffu;
-      }
+  for (int c0 = 0; c0 < nact; c0 += kChunk) {
+    const int cn = min(kChunk, nact - c0);
+    __syncthreads();  // previous chunk flushed
+    if (lr < cn) {
+      const uint32_t g = a.point_list[range.x + c0 + lr];
+      const float2 xy = a.means2d[g];
+      const float4 co = a.conic[g];
+      int rlo, rhi;
+      bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, pminy, rlo, rhi);
+      s_r0[lr] = make_float4(xy.x, xy.y, co.x, co.y);
+      s_r1[lr] = make_float4(co.z, co.w, a.colors[3 * (size_t)g], a.colors[3 * (size_t)g + 1]);
+      s_r2[lr] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), __int_as_float(rlo),
+                             __int_as_float(rhi));
+      s_id[lr] = g;
     }
-    for (int k = lr; k < 32 * (kSlots + 1); k += kTilePx) (&s_acc[0][0])[k] = 0.0f;
-    float T = a.sampled_t[bucket * kTilePx + lr];
-    const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lr;
-    float ar0 = sar[0] - pc0, ar1 = sar[kTilePx] - pc1, ar2 = sar[2 * kTilePx] - pc2;
+    for (int k = lr; k < kChunk * kSlots; k += kTilePx) (&s_acc[0][0])[k] = 0.0f;
     __syncthreads();
-    const int s0 = b * 32;
-    for (int j = 0; j < 32; ++j) {
+    float T = 0.f, adot = 0.f;
+    for (int j = 0; j < cn; ++j) {
+      const int s = c0 + j;
+      if ((s & 31) == 0) {
+        // bucket start: the forward sample of this pixel
+        const size_t bucket = (size_t)bbm0 + (size_t)(s >> 5);
+        T = a.sampled_t[bucket * kTilePx + lr];
+        const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lr;
+        adot = sar[0] * d0 + sar[kTilePx] * d1 + sar[2 * kTilePx] * d2 - pcd;
+      }
       const float4 r2 = s_r2[j];
       if (__float_as_int(r2.w) < wrow || __float_as_int(r2.z) > wrow + 1) continue;  // warp-uniform
       const float4 r0 = s_r0[j];
@@ -184,7 +188,7 @@ __global__ void __launch_bounds__(kTilePx) raster_bwd_kernel(BwdArgs a) {
       const float dx = r0.x - pfx, dy = r0.y - pfy;
       const float power = splat_power(r0.z, r0.w, r1.x, dx, dy);
       // same decisions as the forward pass (NaN exponents included)
-      bool v = (s0 + j < last) && !(power > 0.0f) && !(power <= r2.y);
+      bool v = (s < last) && !(power > 0.0f) && !(power <= r2.y);
       float G = 0.f, oG = 0.f, alpha = 0.f;
       if (v) {
         G = fgs_expf_neg(power);
@@ -197,32 +201,29 @@ __global__ void __launch_bounds__(kTilePx) raster_bwd_kernel(BwdArgs a) {
 #pragma unroll
       for (int k = 0; k < 16; ++k) p[k] = 0.0f;
       if (v) {
-        const float c0 = r1.z, c1 = r1.w, c2 = r2.x;
+        const float c0c = r1.z, c1c = r1.w, c2c = r2.x;
         const float wgt = alpha * T;
         const float rec = __fdividef(1.0f, 1.0f - alpha);
-        ar0 += wgt * c0;
-        ar1 += wgt * c1;
-        ar2 += wgt * c2;
+        const float cdot = c0c * d0 + c1c * d1 + c2c * d2;
+        adot += wgt * cdot;  // remaining colour after this splat, dotted with dL/dpix
+        const float dL_dalpha = T * cdot + rec * (adot - tfbg);
+        T *= (1.0f - alpha);
         p[kR] = wgt * d0;
         p[kG] = wgt * d1;
         p[kB] = wgt * d2;
-        const float cdot = c0 * d0 + c1 * d1 + c2 * d2;
-        const float adot = ar0 * d0 + ar1 * d1 + ar2 * d2;
-        const float dL_dalpha = T * cdot + rec * (adot - tfbg);
-        T *= (1.0f - alpha);
         if (!(oG > 0.99f)) {
-          const float dL_dG = r1.y * dL_dalpha;
-          const float gdx = G * dx, gdy = G * dy;
-          const float tmp_x = dL_dG * (-gdx * r0.z - gdy * r0.w) * hw;
-          const float tmp_y = dL_dG * (-gdy * r1.x - gdx * r0.w) * hh;
+          const float u = r1.y * dL_dalpha * G;  // dL/dG * G
+          const float tmp_x = -u * (r0.z * dx + r0.w * dy) * hw;
+          const float tmp_y = -u * (r1.x * dy + r0.w * dx) * hh;
           p[kMx] = tmp_x;
           p[kMy] = tmp_y;
           p[kMxAbs] = fabsf(tmp_x);
           p[kMyAbs] = fabsf(tmp_y);
-          const float q = -0.5f * dL_dG;
-          p[kCx] = q * gdx * dx;
-          p[kCy] = q * gdx * dy;
-          p[kCw] = q * gdy * dy;
+          const float q = -0.5f * u;
+          const float qdx = q * dx;
+          p[kCx] = qdx * dx;
+          p[kCy] = qdx * dy;
+          p[kCw] = q * dy * dy;
           p[kOp] = G * dL_dalpha;
         }
       }
@@ -231,28 +232,22 @@ __global__ void __launch_bounds__(kTilePx) raster_bwd_kernel(BwdArgs a) {
       if (!(lane & 1) && slot < kSlots) atomicAdd(&s_acc[j][slot], tot);
     }
     __syncthreads();
-    for (int k = lr; k < 32 * kSlots; k += kTilePx) {
-      const int j = k / kSlots, slot = k % kSlots;
-      const uint32_t g = s_id[j];
-      if (g == 0xffffffffu) continue;
-      const float v = s_acc[j][slot];
-      float* dst;
-      switch (slot) {
-        case kMx: dst = a.dmeans2d + 2 * (size_t)g; break;
-        case kMy: dst = a.dmeans2d + 2 * (size_t)g + 1; break;
-        case kMxAbs: dst = a.dviewspace + 4 * (size_t)g + 2; break;
-        case kMyAbs: dst = a.dviewspace + 4 * (size_t)g + 3; break;
-        case kCx: dst = a.dconic + 4 * (size_t)g; break;
-        case kCy: dst = a.dconic + 4 * (size_t)g + 1; break;
-        case kCw: dst = a.dconic + 4 * (size_t)g + 2; break;
-        case kOp: dst = a.dconic + 4 * (size_t)g + 3; break;
-        case kR: dst = a.dcolors + 3 * (size_t)g; break;
-        case kG: dst = a.dcolors + 3 * (size_t)g + 1; break;
-        default: dst = a.dcolors + 3 * (size_t)g + 2; break;
-      }
-      atomicAdd(dst, v);
-      if (slot == kMx) atomicAdd(a.dviewspace + 4 * (size_t)g, v);
-      if (slot == kMy) atomicAdd(a.dviewspace + 4 * (size_t)g + 1, v);
+    if (lr < cn) {
+      const size_t g = s_id[lr];
+      const float* v = s_acc[lr];
+      atomicAdd(a.dmeans2d + 2 * g, v[kMx]);
+      atomicAdd(a.dmeans2d + 2 * g + 1, v[kMy]);
+      atomicAdd(a.dviewspace + 4 * g, v[kMx]);
+      atomicAdd(a.dviewspace + 4 * g + 1, v[kMy]);
+      atomicAdd(a.dviewspace + 4 * g + 2, v[kMxAbs]);
+      atomicAdd(a.dviewspace + 4 * g + 3, v[kMyAbs]);
+      atomicAdd(a.dconic + 4 * g, v[kCx]);
+      atomicAdd(a.dconic + 4 * g + 1, v[kCy]);
+      atomicAdd(a.dconic + 4 * g + 2, v[kCw]);
+      atomicAdd(a.dconic + 4 * g + 3, v[kOp]);
+      atomicAdd(a.dcolors + 3 * g, v[kR]);
+      atomicAdd(a.dcolors + 3 * g + 1, v[kG]);
+      atomicAdd(a.dcolors + 3 * g + 2, v[kB]);
     }
   }
 }
