@@ -42,6 +42,7 @@ _SIGS = {
     "fgs_duplicate_with_keys": (C.c_int, [_i32, _f, _i32, _i32, _p, _p, _p, _p, _p, _i64, _p, _p, _p]),
     "fgs_sort_workspace_bytes": (_sz, [_i64, _i32]),
     "fgs_sort_pairs": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
+    "fgs_sort_pairs_static": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p]),
     "fgs_tile_prep": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _p]),
     "fgs_rasterize_forward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 18),
     "fgs_rasterize_backward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 20),

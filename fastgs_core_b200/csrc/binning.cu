@@ -13,6 +13,7 @@
 // and clamps its stores to the output. Tile ranges follow
 // fastgs_core/metal/fastgs_tile_prep.metal:10-53.
 #include <cstdio>
+#include <mutex>
 
 #include "../../include/fastgs_b200.h"
 #include "fgs_common.cuh"
@@ -417,3 +418,83 @@ int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorte
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free sort: fgs_sort_pairs on a fixed scratch area that lives in
+// this library's device image instead of caller-provided memory.
+//
+// Some callers cannot allocate device memory when they sort: host
+// applications that load this library as a plug-in under a fixed GPU memory
+// budget and forbid allocation after start-up, and callers that must not pay
+// for (or risk the implicit device synchronisation of) cudaMalloc/cudaFree in
+// the middle of their frame. They pass only their keys and values.
+//
+// The scratch is a file-scope device array sized for kStaticSortMaxKeys keys
+// with up to 64 key bits; every GPU that loads the library holds it (about
+// 15 MB) until the process exits. Its address is looked up once per device,
+// on the first call made with that device current.
+namespace fgs {
+constexpr int64_t kStaticSortMaxKeys = FGS_SORT_STATIC_MAX_KEYS;
+constexpr int64_t kStaticSortParts = (kStaticSortMaxKeys + kPart - 1) / kPart;
+constexpr size_t kStaticSortBytes =
+    ((size_t)kMaxPasses * kRadix * 4 + 255) / 256 * 256 +                     // digit histograms
+    ((size_t)kMaxPasses * kStaticSortParts * kRadix * 4 + 255) / 256 * 256 +  // look-back
+    ((size_t)kMaxPasses * 4 + 255) / 256 * 256 +                              // tickets
+    256 +                                                                      // timeout flag
+    ((size_t)kStaticSortMaxKeys * 8 + 255) / 256 * 256 +                      // ping-pong keys
+    ((size_t)kStaticSortMaxKeys * 4 + 255) / 256 * 256;                       // ping-pong values
+
+static __device__ __align__(256) unsigned char g_sort_scratch[kStaticSortBytes];
+
+static std::mutex g_sort_scratch_mu;
+static void* g_sort_scratch_ptr[64] = {nullptr};
+
+// Device address of g_sort_scratch on the current device (host code may not
+// use the symbol itself: on the host it names a stand-in, not device memory).
+static int sort_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("sort_pairs_static: cudaGetDevice: %s", cudaGetErrorString(e));
+    return FGS_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= 64) {
+    set_error("sort_pairs_static: device ordinal %d out of range", dev);
+    return FGS_ERR_CAPACITY;
+  }
+  std::lock_guard<std::mutex> lk(g_sort_scratch_mu);
+  if (g_sort_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_sort_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      set_error("sort_pairs_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return FGS_ERR_CUDA;
+    }
+    g_sort_scratch_ptr[dev] = ptr;
+  }
+  *out = g_sort_scratch_ptr[dev];
+  return FGS_OK;
+}
+}  // namespace fgs
+
+extern "C" int fgs_sort_pairs_static(int64_t num_rendered, int32_t key_bits,
+                                     const uint64_t* keys_in, const uint32_t* values_in,
+                                     uint64_t* keys_out, uint32_t* values_out, void* stream) {
+  FGS_CHECK_ARG(num_rendered >= 0, "num_rendered must be >= 0");
+  if (num_rendered > fgs::kStaticSortMaxKeys) {
+    fgs::set_error("sort_pairs_static sorts at most %lld keys (its scratch is fixed); got %lld: "
+                   "use fgs_sort_pairs with caller-provided workspace",
+                   (long long)fgs::kStaticSortMaxKeys, (long long)num_rendered);
+    return FGS_ERR_CAPACITY;
+  }
+  FGS_CHECK_ARG(key_bits >= 1 && key_bits <= 64, "key_bits must be in [1, 64]");
+  if (num_rendered == 0) return FGS_OK;
+  void* scratch = nullptr;
+  const int st = fgs::sort_scratch_address(&scratch);
+  if (st != FGS_OK) return st;
+  // fgs_sort_pairs clears the histograms, look-back flags, tickets and the
+  // timeout flag at the start of every call, so leftovers of the previous
+  // call do not matter; the key/value halves need no clearing.
+  return fgs_sort_pairs(num_rendered, key_bits, keys_in, values_in, keys_out, values_out, scratch,
+                        fgs::kStaticSortBytes, stream);
+}

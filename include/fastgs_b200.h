@@ -132,6 +132,25 @@ FGS_API int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * fgs_sort_pairs without any allocation. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory when they sort (a
+ * host application that gives plug-ins a fixed GPU memory budget and forbids
+ * allocation after start-up, or a frame loop that must not call
+ * cudaMalloc/cudaFree). The scratch is a fixed area inside the library's
+ * device image (about 15 MB, held on every GPU that loads the library until
+ * the process exits), so at most FGS_SORT_STATIC_MAX_KEYS keys can be sorted;
+ * larger inputs return FGS_ERR_CAPACITY without launching anything. The first
+ * call on each device looks the area up (make it before any stream capture).
+ * Every call shares that one area: calls that overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller.
+ * Same arguments and results as fgs_sort_pairs otherwise.
+ */
+#define FGS_SORT_STATIC_MAX_KEYS 1048576
+FGS_API int fgs_sort_pairs_static(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,
+                                  const uint32_t* values_in, uint64_t* keys_out,
+                                  uint32_t* values_out, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Tile ranges [T,2] (empty tiles [0,0]) and per-tile bucket counts
  * ceil(n_t / 32); plus, new here, the inclusive scan of bucket counts
  * (per_tile_bucket_offset) and its total into *bucket_sum (device uint64).
