@@ -5,8 +5,9 @@
 One step = one view per GPU (weak scaling over the view batch): preprocess ->
 scan -> duplicate -> onesweep sort -> tile prep -> rasterize forward -> L1 +
 0.2 D-SSIM loss -> rasterize backward -> preprocess backward (+ activations,
-densification statistics) -> [NCCL all-reduce of the 59 gradient floats and
-3 statistics per Gaussian, max of screen radii] -> Adam over all parameters.
+densification statistics) -> [NCCL reduce-scatter of the 59 gradient floats
+per Gaussian, sum of 3 statistics and max of the screen radius] -> Adam on
+this rank's shard of the parameters -> [NCCL all-gather of the parameters].
 Workload: BASELINE config 3 (seeded synthetic scene: 64-component mixture,
 seeded random target images, cameras on a radius-6 orbit). N > 1 runs under
 torchrun, one rank per GPU, NCCL; timings are the max over ranks.
@@ -181,6 +182,9 @@ def main():
     dev = torch.device("cuda", local)
     pg = None
     if world > 1:
+        # keep stdout to the one JSON line (NCCL's version banner goes to stdout)
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=dev)
         pg = dist.group.WORLD
     warmup = max(3, args.warmup)
@@ -217,7 +221,8 @@ def main():
         dist.barrier()
 
     # ---------------- value: everything resident in HBM
-    tr.record = {"rasterize_backward", "rasterize_forward"}
+    tr.record = {"rasterize_backward", "rasterize_forward", "adam", "loss", "reduce", "allgather",
+                 "preprocess_backward_train", "sort", "preprocess"}
     tr.events.clear()
     clocks = ClockSampler(local)
     clocks.start()
@@ -241,6 +246,8 @@ def main():
     launches = (tr.launches - launches0) // args.steps
     bwd_ms = tr.kernel_ms("rasterize_backward")
     fwd_ms = tr.kernel_ms("rasterize_forward")
+    stage_ms = {k: tr.kernel_ms(k) for k in ("preprocess", "sort", "loss", "preprocess_backward_train",
+                                              "adam", "reduce", "allgather")}
     tr.record = set()
     t_max = torch.tensor([ms], device=dev)
     if pg is not None:
@@ -294,7 +301,8 @@ def main():
             "iters_per_s": args.steps / (ms / 1000.0),
             "mpix_per_s": value * P / 1e6,
             "gpu_launches": launches,
-            "kernel_ms": {"rasterize_backward": bwd_ms, "rasterize_forward": fwd_ms},
+            "kernel_ms": {"rasterize_backward": bwd_ms, "rasterize_forward": fwd_ms,
+                          **{k: v for k, v in stage_ms.items() if v is not None}},
             "roofline": {"kernel": "rasterize_backward", "bound": "hbm", "achieved": achieved,
                          "peak": peak, "unit": "GB/s", "frac": (achieved / peak) if achieved else None,
                          "peak_kind": peak_kind, "algorithmic_bytes": bwd_bytes,

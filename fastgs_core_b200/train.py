@@ -5,8 +5,9 @@ buffer (59 floats per Gaussian; layout in include/fastgs_b200.h). A step takes
 a batch of cameras; rank r renders views r, r+R, ... through the rasterizer
 kernels, back-propagates an L1 + D-SSIM loss into the flat gradient buffer
 (activations fused into preprocess-backward), all-reduces the gradients and
-densification statistics over NCCL (one sum over 62N floats, one max over
-the N per-Gaussian screen radii), and applies Adam on every rank.
+densification statistics over NCCL (a reduce-scatter of the 59N gradient
+floats, a sum of 3N statistics and a max of the N screen radii), applies
+Adam to its 1/R shard of the parameters and all-gathers the shards.
 
 This is the trainer loop of scripts/train_scanner_fastgs.py:968-1019 (one
 loss per view, Adam with per-group learning rates, densification statistics
@@ -67,16 +68,39 @@ def local_views(num_views: int, world: int, rank: int) -> list[int]:
     return list(range(rank, num_views, world))
 
 
-def allreduce_step(step_buf: torch.Tensor, n: int, group=None) -> None:
-    """Combine one step's per-rank buffers in place: sum over the 59N
-    gradient floats and the 3N summed statistics, max over the last N (screen
-    radii). Works for any torch.distributed backend (NCCL on GPUs, gloo on
-    CPU)."""
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Slice [lo, hi) of a flat buffer of ``total`` floats owned by ``rank``
+    when it is padded to a multiple of 4 * world (16-byte aligned shards)."""
+    per = -(-total // (4 * world)) * 4
+    lo = min(total, rank * per)
+    return lo, min(total, lo + per)
+
+
+def reduce_scatter_grads(padded: torch.Tensor, world: int, rank: int, group=None) -> torch.Tensor:
+    """Sum the per-rank gradient buffers and leave this rank its shard, in
+    place (``padded`` has a 4*world-aligned length; returns the shard view)."""
     import torch.distributed as dist
 
-    split = (FLOATS_PER_GAUSSIAN + STATS_SUM) * n
-    dist.all_reduce(step_buf[:split], group=group)
-    dist.all_reduce(step_buf[split:split + n], op=dist.ReduceOp.MAX, group=group)
+    per = padded.numel() // world
+    shard = padded[rank * per:(rank + 1) * per]
+    dist.reduce_scatter_tensor(shard, padded, group=group)
+    return shard
+
+
+def allgather_params(padded: torch.Tensor, world: int, rank: int, group=None) -> None:
+    """Every rank's updated parameter shard into every rank's full buffer (in place)."""
+    import torch.distributed as dist
+
+    per = padded.numel() // world
+    dist.all_gather_into_tensor(padded, padded[rank * per:(rank + 1) * per], group=group)
+
+
+def allreduce_stats(step_stats: torch.Tensor, n: int, group=None) -> None:
+    """Sum of the 3N densification statistics, max of the N screen radii."""
+    import torch.distributed as dist
+
+    dist.all_reduce(step_stats[: STATS_SUM * n], group=group)
+    dist.all_reduce(step_stats[STATS_SUM * n:STATS_SUM * n + n], op=dist.ReduceOp.MAX, group=group)
 
 
 def fold_stats(stats: torch.Tensor, step_stats: torch.Tensor, n: int) -> None:
@@ -108,18 +132,32 @@ class Trainer:
                                scene.log_scales.reshape(-1), scene.rotations.reshape(-1)]).astype(np.float32)
         assert flat.size == FLOATS_PER_GAUSSIAN * n
         d = self.dev
-        self.params = torch.from_numpy(flat).to(d)
-        # one buffer per step: gradients (59N), this step's densification
-        # statistics (sum |grad_xy|, sum |grad_abs|, views: 3N, summed across
-        # ranks) and the step's max screen radius (N, max across ranks)
-        self.step_buf = torch.zeros((FLOATS_PER_GAUSSIAN + STATS_SUM + 1) * n, device=d)
-        self.grads = self.step_buf[: FLOATS_PER_GAUSSIAN * n]
-        self.step_stats = self.step_buf[FLOATS_PER_GAUSSIAN * n:]
+        self.world, self.rank = 1, 0
+        if process_group is not None:
+            import torch.distributed as dist
+
+            self.world, self.rank = dist.get_world_size(process_group), dist.get_rank(process_group)
+        total = FLOATS_PER_GAUSSIAN * n
+        # parameters and gradients padded to 16-byte-aligned equal shards: with
+        # several ranks the gradients are reduce-scattered, each rank runs Adam
+        # on its shard only and the parameters are all-gathered back
+        self._per = -(-total // (4 * self.world)) * 4
+        padded = self._per * self.world
+        self.params_pad = torch.zeros(padded, device=d)
+        self.params_pad[:total].copy_(torch.from_numpy(flat))
+        self.params = self.params_pad[:total]
+        self.grads_pad = torch.zeros(padded, device=d)
+        self.grads = self.grads_pad[:total]
+        self._lo, self._hi = shard_range(total, self.world, self.rank)
+        # this step's densification statistics: sum |grad_xy|, sum |grad_abs|,
+        # visible-view count (3N, summed across ranks), max screen radius (N, max)
+        self.step_stats = torch.zeros((STATS_SUM + 1) * n, device=d)
         # running densification statistics [acc, acc_abs, denom, max_radii]
         # (FastGSDensificationState of scripts/train_scanner_fastgs.py)
         self.stats = torch.zeros(4 * n, device=d)
-        self.exp_avg = torch.zeros_like(self.params)
-        self.exp_avg_sq = torch.zeros_like(self.params)
+        # Adam moments of this rank's shard
+        self.exp_avg = torch.zeros(self._per, device=d)
+        self.exp_avg_sq = torch.zeros(self._per, device=d)
         self.opacities = torch.empty(n, device=d)
         self.scales = torch.empty((n, 3), device=d)
         self.quats = torch.empty((n, 4), device=d)
@@ -129,7 +167,9 @@ class Trainer:
         self.k_host = torch.empty(1, dtype=torch.uint64, pin_memory=True)
         self.last_rendered = 0
         self.last_buckets_bound = 0
-        ends = np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n
+        # learning-rate group ends, relative to this rank's shard
+        ends = np.clip(np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n - self._lo, 0,
+                       self._hi - self._lo)
         self._group_end = (C.c_int64 * 6)(*ends.tolist())
         # instrumentation: CUDA events around chosen launches (same stream),
         # and a count of this library's kernel launches
@@ -152,6 +192,18 @@ class Trainer:
             ev[1].record()
             self.events.setdefault(name, []).append(ev)
         self.launches += self._KERNELS.get(name, 0)
+
+    def _begin(self, name):
+        if name not in self.record:
+            return None
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
+        return ev
+
+    def _end(self, name, ev):
+        if ev is not None:
+            ev[1].record()
+            self.events.setdefault(name, []).append(ev)
 
     def kernel_ms(self, name):
         """Mean duration (ms) of the recorded launches of ``name``; clears them."""
@@ -292,11 +344,7 @@ class Trainer:
         renders its share). ``targets[i]`` is the [3, H*W] float32 target of
         cams[i] on this device (None for views of other ranks). The loss of
         the local views (sum) lands in loss_out[0] (device)."""
-        world, rank = 1, 0
-        if self.pg is not None:
-            import torch.distributed as dist
-
-            world, rank = dist.get_world_size(self.pg), dist.get_rank(self.pg)
+        world, rank = self.world, self.rank
         mine = local_views(len(cams), world, rank)
         self.activate()
         self.step_stats.zero_()
@@ -310,14 +358,22 @@ class Trainer:
             self.render_view(cams[v], targets[v], accumulate=j > 0, loss_out=lo, loss_scale=scale)
             if loss_out is not None and j > 0:
                 loss_out[:3].add_(lo[:3])
+        lo, hi = self._lo, self._hi
         if world > 1:
-            allreduce_step(self.step_buf, self.n, self.pg)
+            ev = self._begin("reduce")
+            reduce_scatter_grads(self.grads_pad, world, rank, self.pg)
+            allreduce_stats(self.step_stats, self.n, self.pg)
+            self._end("reduce", ev)
         fold_stats(self.stats, self.step_stats, self.n)
         self.step_count += 1
         lr = self.lrs
         lrs = (C.c_float * 6)(lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations)
-        self._call("adam", lib().fgs_adam_step, self.params.numel(), _p(self.params), _p(self.grads),
-                   _p(self.exp_avg), _p(self.exp_avg_sq), 6, self._group_end, lrs,
-                   float(self.betas[0]), float(self.betas[1]), self.eps, self.step_count,
-                   int(self.bias_correction), self._stream())
+        self._call("adam", lib().fgs_adam_step, hi - lo, _p(self.params_pad[lo:]),
+                   _p(self.grads_pad[lo:]), _p(self.exp_avg), _p(self.exp_avg_sq), 6,
+                   self._group_end, lrs, float(self.betas[0]), float(self.betas[1]), self.eps,
+                   self.step_count, int(self.bias_correction), self._stream())
+        if world > 1:
+            ev = self._begin("allgather")
+            allgather_params(self.params_pad, world, rank, self.pg)
+            self._end("allgather", ev)
         return len(mine)
