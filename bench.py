@@ -221,7 +221,7 @@ def main():
         dist.barrier()
 
     # ---------------- value: everything resident in HBM
-    tr.record = {"rasterize_backward", "rasterize_forward", "adam", "loss", "reduce", "allgather",
+    tr.record = {"rasterize_backward", "rasterize_forward", "adam", "loss", "reduce", "allgather", "exchange",
                  "preprocess_backward_train", "sort", "preprocess"}
     tr.events.clear()
     clocks = ClockSampler(local)
@@ -247,7 +247,7 @@ def main():
     bwd_ms = tr.kernel_ms("rasterize_backward")
     fwd_ms = tr.kernel_ms("rasterize_forward")
     stage_ms = {k: tr.kernel_ms(k) for k in ("preprocess", "sort", "loss", "preprocess_backward_train",
-                                              "adam", "reduce", "allgather")}
+                                              "adam", "reduce", "allgather", "exchange")}
     tr.record = set()
     t_max = torch.tensor([ms], device=dev)
     if pg is not None:
@@ -296,6 +296,7 @@ def main():
             "config": {"workload": WORKLOAD, "model": "3DGS/FastGS rasterizer", "global_batch": world,
                        "seq_len": None, "parallelism": f"dp{world} (view-sharded)",
                        "gaussians": n, "image": f"{W}x{H}", "views_per_gpu_per_step": 1,
+                       "exchange": tr.comm,
                        "l2": "inputs larger than L2 (params+Adam state 944 MB)",
                        "mean_keys_per_view": K},
             "iters_per_s": args.steps / (ms / 1000.0),

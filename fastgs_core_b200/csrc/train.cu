@@ -268,6 +268,64 @@ __global__ void adam_kernel(int64_t total, float* __restrict__ p, const float* _
   }
 }
 
+
+// ------------------------------------------- Adam fused with the exchange
+// Data-parallel update of one rank's parameter shard over NVLink multicast
+// (NVLS): the summed gradient of the shard is read with multimem.ld_reduce
+// (the NVSwitch adds every rank's copy), Adam runs on it, and the updated
+// parameters are written to every rank's copy with one multimem.st. This
+// replaces reduce-scatter + Adam + all-gather: the gradient reads use each
+// GPU's NVLink egress and the parameter broadcast its ingress, so the two
+// halves of the exchange overlap instead of running back to back.
+__device__ __forceinline__ float4 mc_ld_reduce_add(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mc_store(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(256)
+    adam_nvls_kernel(int64_t total4, const float* __restrict__ p_local, float* p_mc,
+                     const float* g_mc, float* __restrict__ m, float* __restrict__ v,
+                     AdamGroups grp, float b1, float b2, float eps, float bc1, float bc2) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4; i4 += stride) {
+    const float4 gg = mc_ld_reduce_add(g_mc + 4 * i4);
+    float4 pp = reinterpret_cast<const float4*>(p_local)[i4];
+    float4 mm = reinterpret_cast<float4*>(m)[i4];
+    float4 vv = reinterpret_cast<float4*>(v)[i4];
+    float* pa = &pp.x;
+    const float* ga = &gg.x;
+    float* ma = &mm.x;
+    float* va = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int64_t idx = 4 * i4 + k;
+      float lr = grp.lr[grp.count - 1];
+      for (int q = 0; q < grp.count; ++q)
+        if (idx < grp.end[q]) {
+          lr = grp.lr[q];
+          break;
+        }
+      ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
+      va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
+      pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
+    }
+    reinterpret_cast<float4*>(m)[i4] = mm;
+    reinterpret_cast<float4*>(v)[i4] = vv;
+    mc_store(p_mc + 4 * i4, pp);
+  }
+  // make the broadcast visible system-wide before the caller's barrier
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 // ------------------------------------------------------------ FastGS scores
 // scripts/train_scanner_fastgs.py:262-340
 __global__ void l1_map_kernel(int64_t P, const float* __restrict__ pred,
@@ -434,6 +492,43 @@ int fgs_adam_step(int64_t total, float* params, const float* grads, float* exp_a
   adam_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
       total, params, grads, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
   return check_launch("adam_step");
+}
+
+int fgs_adam_step_multicast(int64_t shard, const float* params_local, float* params_mc,
+                            const float* grads_mc, float* exp_avg, float* exp_avg_sq,
+                            int32_t num_groups, const int64_t* group_end, const float* group_lr,
+                            float beta1, float beta2, float eps, int32_t step,
+                            int32_t bias_correction, void* stream) {
+  FGS_CHECK_ARG(shard >= 0 && shard % 4 == 0, "shard length must be a multiple of 4");
+  FGS_CHECK_ARG(num_groups >= 1 && num_groups <= 8, "num_groups must be in [1, 8]");
+  FGS_CHECK_ARG(group_end && group_lr, "missing group table");
+  if (shard == 0) return FGS_OK;
+  FGS_CHECK_ARG(params_local && params_mc && grads_mc && exp_avg && exp_avg_sq, "missing pointer");
+  FGS_CHECK_ARG(((uintptr_t)params_local | (uintptr_t)params_mc | (uintptr_t)grads_mc |
+                 (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq) % 16 == 0,
+                "buffers must be 16-byte aligned");
+  AdamGroups g;
+  memset(&g, 0, sizeof(g));
+  g.count = num_groups;
+  for (int k = 0; k < num_groups; ++k) {
+    g.end[k] = group_end[k];
+    g.lr[k] = group_lr[k];
+  }
+  float bc1 = 1.f, bc2 = 1.f;
+  if (bias_correction) {
+    FGS_CHECK_ARG(step >= 1, "step must be >= 1 with bias correction");
+    bc1 = 1.0f / (1.0f - powf(beta1, (float)step));
+    bc2 = 1.0f / (1.0f - powf(beta2, (float)step));
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n4 = shard / 4;
+  const int64_t want = (n4 + 255) / 256;
+  const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  adam_nvls_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+      n4, params_local, params_mc, grads_mc, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
+  return check_launch("adam_step_multicast");
 }
 
 int fgs_metric_map(int64_t num_pixels, const float* pred, const float* target, float loss_thresh,

@@ -5,9 +5,12 @@ buffer (59 floats per Gaussian; layout in include/fastgs_b200.h). A step takes
 a batch of cameras; rank r renders views r, r+R, ... through the rasterizer
 kernels, back-propagates an L1 + D-SSIM loss into the flat gradient buffer
 (activations fused into preprocess-backward), all-reduces the gradients and
-densification statistics over NCCL (a reduce-scatter of the 59N gradient
-floats, a sum of 3N statistics and a max of the N screen radii), applies
-Adam to its 1/R shard of the parameters and all-gathers the shards.
+then updates its 1/R shard of the parameters. With NVLink multicast (the
+default where symmetric memory supports it) one kernel reads the rank-summed
+shard gradient from the switch, runs Adam and broadcasts the new parameters
+to every rank (fgs_adam_step_multicast); otherwise NCCL reduce-scatters the
+gradients and all-gathers the parameter shards around a local Adam.
+Densification statistics stay per rank and are combined on demand.
 
 This is the trainer loop of scripts/train_scanner_fastgs.py:968-1019 (one
 loss per view, Adam with per-group learning rates, densification statistics
@@ -18,6 +21,7 @@ statistics come from the render the loss is taken on.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -61,6 +65,28 @@ class _Grow:
             t = torch.empty(max(int(numel * 1.15), 1024), dtype=dtype, device=self.dev)
             self.b[name] = t
         return t[:numel]
+
+
+def _symmetric_pair(numel: int, dev, group):
+    """Parameter and gradient buffers in symmetric memory bound to an NVLink
+    multicast object (None where that is unavailable)."""
+    try:
+        import torch.distributed._symmetric_memory as symm
+    except ImportError:
+        return None
+    try:
+        name = group.group_name if group is not None else "0"
+        if hasattr(symm, "enable_symm_mem_for_group"):
+            symm.enable_symm_mem_for_group(name)
+        p = symm.empty(numel, dtype=torch.float32, device=dev)
+        g = symm.empty(numel, dtype=torch.float32, device=dev)
+        hp = symm.rendezvous(p, name)
+        hg = symm.rendezvous(g, name)
+        if not getattr(hp, "multicast_ptr", 0) or not getattr(hg, "multicast_ptr", 0):
+            return None
+        return p, g, hp, hg
+    except Exception:
+        return None
 
 
 def local_views(num_views: int, world: int, rank: int) -> list[int]:
@@ -117,7 +143,8 @@ class Trainer:
 
     def __init__(self, scene, device, lrs: LearningRates | None = None, w_l1: float = 1.0,
                  w_ssim: float = 0.2, betas=(0.9, 0.99), eps: float = 1e-8,
-                 bias_correction: bool = False, process_group=None, background=(0.0, 0.0, 0.0)):
+                 bias_correction: bool = False, process_group=None, background=(0.0, 0.0, 0.0),
+                 comm: str | None = None):
         self.dev = torch.device(device)
         self.n = n = int(scene.means3d.shape[0])
         if scene.features_rest.shape[1:] != (15, 3):
@@ -143,17 +170,32 @@ class Trainer:
         # on its shard only and the parameters are all-gathered back
         self._per = -(-total // (4 * self.world)) * 4
         padded = self._per * self.world
-        self.params_pad = torch.zeros(padded, device=d)
+        self.comm = "local"
+        self._symm = None
+        if self.world > 1:
+            self.comm = comm or os.environ.get("FGS_COMM", "") or "multicast"
+            if self.comm == "multicast":
+                self._symm = _symmetric_pair(padded, d, process_group)
+                if self._symm is None:
+                    self.comm = "nccl"
+        if self._symm is not None:
+            self.params_pad, self.grads_pad, self._hp, self._hg = self._symm
+            self.params_pad.zero_()
+            self.grads_pad.zero_()
+        else:
+            self.params_pad = torch.zeros(padded, device=d)
+            self.grads_pad = torch.zeros(padded, device=d)
         self.params_pad[:total].copy_(torch.from_numpy(flat))
         self.params = self.params_pad[:total]
-        self.grads_pad = torch.zeros(padded, device=d)
         self.grads = self.grads_pad[:total]
         self._lo, self._hi = shard_range(total, self.world, self.rank)
-        # this step's densification statistics: sum |grad_xy|, sum |grad_abs|,
-        # visible-view count (3N, summed across ranks), max screen radius (N, max)
+        # this step's densification statistics of this rank's views: sum
+        # |grad_xy|, sum |grad_abs|, visible-view count (3N), max screen radius (N)
         self.step_stats = torch.zeros((STATS_SUM + 1) * n, device=d)
-        # running densification statistics [acc, acc_abs, denom, max_radii]
-        # (FastGSDensificationState of scripts/train_scanner_fastgs.py)
+        # running densification statistics of this rank [acc, acc_abs, denom,
+        # max_radii] (FastGSDensificationState of scripts/train_scanner_fastgs.py).
+        # Sums and maxima commute, so ranks keep their own and global_stats()
+        # combines them when densification needs them: no per-step collective.
         self.stats = torch.zeros(4 * n, device=d)
         # Adam moments of this rank's shard
         self.exp_avg = torch.zeros(self._per, device=d)
@@ -334,6 +376,14 @@ class Trainer:
             _p(self.grads), _p(self.step_stats), st)
         return img
 
+    def global_stats(self) -> torch.Tensor:
+        """Densification statistics over every rank's views (sum; max for the
+        screen radius), as a new tensor [acc, acc_abs, denom, max_radii]."""
+        out = self.stats.clone()
+        if self.world > 1:
+            allreduce_stats(out, self.n, self.pg)
+        return out
+
     # -- full step --------------------------------------------------------
     def activate(self):
         self._call("activate", lib().fgs_activate_params, self.n, _p(self.params), _p(self.opacities),
@@ -359,19 +409,33 @@ class Trainer:
             if loss_out is not None and j > 0:
                 loss_out[:3].add_(lo[:3])
         lo, hi = self._lo, self._hi
-        if world > 1:
-            ev = self._begin("reduce")
-            reduce_scatter_grads(self.grads_pad, world, rank, self.pg)
-            allreduce_stats(self.step_stats, self.n, self.pg)
-            self._end("reduce", ev)
         fold_stats(self.stats, self.step_stats, self.n)
         self.step_count += 1
         lr = self.lrs
         lrs = (C.c_float * 6)(lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations)
+        b1, b2 = float(self.betas[0]), float(self.betas[1])
+        if self.comm == "multicast":
+            # every rank's gradients written -> fused exchange + Adam -> every
+            # rank's parameter broadcast landed (also guards the next step's
+            # gradient writes against peers still reading these)
+            ev = self._begin("exchange")
+            self._hp.barrier(channel=0)
+            off = lo * 4
+            self._call("adam", lib().fgs_adam_step_multicast, self._per, _p(self.params_pad[lo:]),
+                       C.c_void_p(self._hp.multicast_ptr + off), C.c_void_p(self._hg.multicast_ptr + off),
+                       _p(self.exp_avg), _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2,
+                       self.eps, self.step_count, int(self.bias_correction), self._stream())
+            self._hp.barrier(channel=1)
+            self._end("exchange", ev)
+            return len(mine)
+        if world > 1:
+            ev = self._begin("reduce")
+            reduce_scatter_grads(self.grads_pad, world, rank, self.pg)
+            self._end("reduce", ev)
         self._call("adam", lib().fgs_adam_step, hi - lo, _p(self.params_pad[lo:]),
                    _p(self.grads_pad[lo:]), _p(self.exp_avg), _p(self.exp_avg_sq), 6,
-                   self._group_end, lrs, float(self.betas[0]), float(self.betas[1]), self.eps,
-                   self.step_count, int(self.bias_correction), self._stream())
+                   self._group_end, lrs, b1, b2, self.eps, self.step_count,
+                   int(self.bias_correction), self._stream())
         if world > 1:
             ev = self._begin("allgather")
             allgather_params(self.params_pad, world, rank, self.pg)

@@ -292,6 +292,22 @@ FGS_API int fgs_adam_step(int64_t total, float* params, const float* grads, floa
                           const float* group_lr, float beta1, float beta2, float eps, int32_t step,
                           int32_t bias_correction, void* stream);
 
+/* Data-parallel Adam over NVLink multicast (new here; the reference is single-
+ * device). The gradient and parameter buffers are symmetric allocations bound
+ * to an NVLink multicast object on every rank (e.g. torch symmetric memory);
+ * grads_mc / params_mc are the multicast addresses of this rank's shard,
+ * params_local its local copy, exp_avg / exp_avg_sq this rank's moments
+ * (shard floats, multiple of 4). The kernel reads the rank-summed gradient with
+ * multimem.ld_reduce, applies the Adam rule of fgs_adam_step, and stores the
+ * new parameters to every rank with multimem.st. Callers bracket it with a
+ * cross-rank barrier before (all gradients written) and after (all stores
+ * visible). Group ends are relative to the shard. */
+FGS_API int fgs_adam_step_multicast(int64_t shard, const float* params_local, float* params_mc,
+                                    const float* grads_mc, float* exp_avg, float* exp_avg_sq,
+                                    int32_t num_groups, const int64_t* group_end,
+                                    const float* group_lr, float beta1, float beta2, float eps,
+                                    int32_t step, int32_t bias_correction, void* stream);
+
 /* FastGS multi-view score pass (scripts/train_scanner_fastgs.py:262-340):
  * fgs_metric_map: per-pixel mean |pred - target| over channels, min-max
  *   normalised, > loss_thresh -> metric_map [P] int32; *l1_sum (device) gets
