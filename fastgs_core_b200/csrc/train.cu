@@ -291,36 +291,55 @@ __device__ __forceinline__ void mc_store(float* mc, float4 v) {
                : "memory");
 }
 
+__device__ __forceinline__ void adam4(float4& pp, float4& mm, float4& vv, const float4 gg,
+                                      int64_t idx0, const AdamGroups& grp, float b1, float b2,
+                                      float eps, float bc1, float bc2) {
+  float* pa = &pp.x;
+  const float* ga = &gg.x;
+  float* ma = &mm.x;
+  float* va = &vv.x;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int64_t idx = idx0 + k;
+    float lr = grp.lr[grp.count - 1];
+    for (int q = 0; q < grp.count; ++q)
+      if (idx < grp.end[q]) {
+        lr = grp.lr[q];
+        break;
+      }
+    ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
+    va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
+    pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
+  }
+}
+
+constexpr int kMcUnroll = 4;  // independent multicast loads in flight per thread
+
 __global__ void __launch_bounds__(256)
     adam_nvls_kernel(int64_t total4, const float* __restrict__ p_local, float* p_mc,
                      const float* g_mc, float* __restrict__ m, float* __restrict__ v,
                      AdamGroups grp, float b1, float b2, float eps, float bc1, float bc2) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4; i4 += stride) {
-    const float4 gg = mc_ld_reduce_add(g_mc + 4 * i4);
-    float4 pp = reinterpret_cast<const float4*>(p_local)[i4];
-    float4 mm = reinterpret_cast<float4*>(m)[i4];
-    float4 vv = reinterpret_cast<float4*>(v)[i4];
-    float* pa = &pp.x;
-    const float* ga = &gg.x;
-    float* ma = &mm.x;
-    float* va = &vv.x;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t base = t; base < total4; base += stride * kMcUnroll) {
+    float4 gg[kMcUnroll];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int64_t idx = 4 * i4 + k;
-      float lr = grp.lr[grp.count - 1];
-      for (int q = 0; q < grp.count; ++q)
-        if (idx < grp.end[q]) {
-          lr = grp.lr[q];
-          break;
-        }
-      ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
-      va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
-      pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
+    for (int u = 0; u < kMcUnroll; ++u) {
+      const int64_t i4 = base + u * stride;
+      if (i4 < total4) gg[u] = mc_ld_reduce_add(g_mc + 4 * i4);
     }
-    reinterpret_cast<float4*>(m)[i4] = mm;
-    reinterpret_cast<float4*>(v)[i4] = vv;
-    mc_store(p_mc + 4 * i4, pp);
+#pragma unroll
+    for (int u = 0; u < kMcUnroll; ++u) {
+      const int64_t i4 = base + u * stride;
+      if (i4 >= total4) break;
+      float4 pp = reinterpret_cast<const float4*>(p_local)[i4];
+      float4 mm = reinterpret_cast<float4*>(m)[i4];
+      float4 vv = reinterpret_cast<float4*>(v)[i4];
+      adam4(pp, mm, vv, gg[u], 4 * i4, grp, b1, b2, eps, bc1, bc2);
+      reinterpret_cast<float4*>(m)[i4] = mm;
+      reinterpret_cast<float4*>(v)[i4] = vv;
+      mc_store(p_mc + 4 * i4, pp);
+    }
   }
   // make the broadcast visible system-wide before the caller's barrier
   asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -525,7 +544,7 @@ int fgs_adam_step_multicast(int64_t shard, const float* params_local, float* par
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t n4 = shard / 4;
   const int64_t want = (n4 + 255) / 256;
-  const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  const int blocks = (int)(want < (int64_t)sms * 4 ? want : (int64_t)sms * 4);
   adam_nvls_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
       n4, params_local, params_mc, grads_mc, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
   return check_launch("adam_step_multicast");
