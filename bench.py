@@ -255,18 +255,43 @@ def main():
     ms = float(t_max.item())
 
     # ---------------- e2e: public API with host buffers every step
-    targ = torch.empty((3, P), device=dev)
+    # the target of step s+1 is copied from pinned host memory on a copy
+    # stream while step s computes (double buffer); the loss comes back each step
     loss_host = torch.empty(4, pin_memory=True)
-    for s in range(3):
-        one_step(s, lambda i: targ.copy_(host_targets[i], non_blocking=True))
+    copy_stream = torch.cuda.Stream(device=dev)
+    tbuf = [torch.empty((3, P), device=dev) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    cur = torch.cuda.current_stream(dev)
+
+    def prefetch(step):
+        k = step % 2
+        _, idx = batch(step)
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(freed[k])
+            tbuf[k].copy_(host_targets[idx[rank]], non_blocking=True)
+            ready[k].record(copy_stream)
+
+    def e2e_steps(first, count):
+        prefetch(first)
+        for s in range(first, first + count):
+            k = s % 2
+            if s + 1 < first + count:
+                prefetch(s + 1)
+            cur.wait_event(ready[k])
+            one_step(s, lambda i, k=k: tbuf[k])
+            freed[k].record(cur)
+            loss_host.copy_(loss_dev, non_blocking=True)
+
+    for k in range(2):
+        freed[k].record(cur)
+    e2e_steps(0, 3)
     torch.cuda.synchronize()
     if pg is not None:
         dist.barrier()
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record()
-    for s in range(args.steps):
-        one_step(warmup + s, lambda i: targ.copy_(host_targets[i], non_blocking=True))
-        loss_host.copy_(loss_dev, non_blocking=True)
+    e2e_steps(warmup, args.steps)
     e3.record()
     torch.cuda.synchronize()
     ms_e2e = e2.elapsed_time(e3)

@@ -284,9 +284,15 @@ class Trainer:
         T = gx * gy
         st = self._stream()
         cm = ws.get("cam", 35, torch.float32)
-        cm.copy_(torch.from_numpy(np.concatenate([cam.viewmatrix.reshape(-1), cam.projmatrix.reshape(-1),
-                                                  cam.campos.reshape(-1)]).astype(np.float32)),
-                 non_blocking=True)
+        # pinned staging: the previous view's copy has completed by now (each
+        # view synchronises once on its key count)
+        if not hasattr(self, "_cam_host"):
+            self._cam_host = torch.empty(35, dtype=torch.float32, pin_memory=True)
+        hc = self._cam_host.numpy()
+        hc[0:16] = cam.viewmatrix.reshape(-1)
+        hc[16:32] = cam.projmatrix.reshape(-1)
+        hc[32:35] = cam.campos.reshape(-1)
+        cm.copy_(self._cam_host, non_blocking=True)
         vm, pm, cp = cm[0:16], cm[16:32], cm[32:35]
         prm = PreprocessParams(n, self.sh_degree, 15, 1.0, 1.0, float(cam.tan_fovx), float(cam.tan_fovy),
                                W, H, 0, 0)
