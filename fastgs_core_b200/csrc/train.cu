@@ -35,90 +35,202 @@ __global__ void activate_kernel(int64_t n, const float* __restrict__ flat, float
 // C2 = 0.03^2; loss = w_l1 * mean|x - y| + w_ssim * (1 - mean SSIM(x, y)) over
 // the 3 x H x W image (x = render, y = target, both CHW).
 constexpr int kR = 5;
-constexpr int kT = 16;
-constexpr int kS = kT + 2 * kR;  // 26
 __constant__ float c_win[11];
 
+// Fused L1 + D-SSIM forward and backward: one CTA per 32x32 output tile and
+// channel. The CTA loads its 52x52 input window once, forms the five local
+// moments by separable 11-tap convolution, evaluates SSIM and its partial
+// derivatives (dS/dmu_x, dS/dE[x^2], dS/dE[xy]) on the 42x42 region the
+// backward convolution needs (recomputing the 5-pixel halo instead of writing
+// and re-reading global maps), convolves them back and writes dL/dimage.
+constexpr int kFO = 32;               // output tile
+constexpr int kFM = kFO + 2 * kR;     // 42: derivative-map region
+constexpr int kFI = kFM + 2 * kR;     // 52: input region
+// shared memory: region A holds the input window, then (aliased) the
+// derivative maps; region B the horizontal moments, then the second pass
+constexpr int kRegionA = 2 * kFI * (kFI + 1);
+constexpr int kRegionB = 5 * kFI * kFM;
+static_assert(3 * kFM * (kFM + 1) <= kRegionA, "maps must fit the input region");
+static_assert(3 * kFM * kFO <= kRegionB, "second pass must fit the moment region");
+constexpr int kFusedSmemFloats = kRegionA + kRegionB;
+
 __global__ void __launch_bounds__(256)
-    ssim_fwd_kernel(int W, int H, const float* __restrict__ x, const float* __restrict__ y,
-                    float* __restrict__ maps, float* __restrict__ partials) {
-  __shared__ float s_x[kS][kS + 1];
-  __shared__ float s_y[kS][kS + 1];
-  __shared__ float s_h[5][kS][kT + 1];
+    ssim_fused_kernel(int W, int H, const float* __restrict__ x, const float* __restrict__ y,
+                      float w_l1_n, float w_ssim_n, float* __restrict__ dx,
+                      float* __restrict__ partials) {
+  extern __shared__ float sm[];
+  float* sx = sm;                    // [kFI][kFI+1]   (region A)
+  float* sy = sx + kFI * (kFI + 1);  // [kFI][kFI+1]   (region A)
+  float* sh = sm + kRegionA;         // [5][kFI][kFM]  (region B)
+  float* mp = sm;                    // [3][kFM][kFM+1] over region A, after the moments
+  float* h2 = sm + kRegionA;         // [3][kFM][kFO]  over region B, after the maps
   __shared__ float s_red[2][8];
-  const int tx0 = blockIdx.x * kT, ty0 = blockIdx.y * kT;
-  const int c = blockIdx.z;
+  const int x0 = blockIdx.x * kFO, y0 = blockIdx.y * kFO, c = blockIdx.z;
   const size_t P = (size_t)W * H;
   const float* xc = x + c * P;
   const float* yc = y + c * P;
   const int t = threadIdx.x;
-  for (int k = t; k < kS * kS; k += 256) {
-    const int r = k / kS, q = k % kS;
-    const int gy = ty0 - kR + r, gx = tx0 - kR + q;
+  for (int k = t; k < kFI * kFI; k += 256) {
+    const int r = k / kFI, q = k % kFI;
+    const int gy = y0 - 2 * kR + r, gx = x0 - 2 * kR + q;
     const bool in = gx >= 0 && gx < W && gy >= 0 && gy < H;
-    s_x[r][q] = in ? xc[(size_t)gy * W + gx] : 0.0f;
-    s_y[r][q] = in ? yc[(size_t)gy * W + gx] : 0.0f;
+    sx[r * (kFI + 1) + q] = in ? xc[(size_t)gy * W + gx] : 0.0f;
+    sy[r * (kFI + 1) + q] = in ? yc[(size_t)gy * W + gx] : 0.0f;
   }
   __syncthreads();
-  for (int k = t; k < kS * kT; k += 256) {
-    const int r = k / kT, q = k % kT;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+  // horizontal moments: each item is a row segment of kSeg outputs computed
+  // from one sliding window of kSeg + 10 inputs held in registers
+  constexpr int kSeg = 6;
+  constexpr int kHSeg = kFM / kSeg;  // 7 segments of 6 over 42 columns
+  for (int k = t; k < kFI * kHSeg; k += 256) {
+    const int r = k / kHSeg, q0 = (k % kHSeg) * kSeg;
+    float xv[kSeg + 10], yv[kSeg + 10];
 #pragma unroll
-    for (int j = 0; j < 11; ++j) {
-      const float w = c_win[j], xv = s_x[r][q + j], yv = s_y[r][q + j];
-      a0 += w * xv;
-      a1 += w * yv;
-      a2 += w * xv * xv;
-      a3 += w * yv * yv;
-      a4 += w * xv * yv;
+    for (int i = 0; i < kSeg + 10; ++i) {
+      xv[i] = sx[r * (kFI + 1) + q0 + i];
+      yv[i] = sy[r * (kFI + 1) + q0 + i];
     }
-    s_h[0][r][q] = a0;
-    s_h[1][r][q] = a1;
-    s_h[2][r][q] = a2;
-    s_h[3][r][q] = a3;
-    s_h[4][r][q] = a4;
+#pragma unroll
+    for (int o = 0; o < kSeg; ++o) {
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 11; ++j) {
+        const float w = c_win[j], xx = xv[o + j], yy = yv[o + j];
+        a0 += w * xx;
+        a1 += w * yy;
+        a2 += w * xx * xx;
+        a3 += w * yy * yy;
+        a4 += w * xx * yy;
+      }
+      sh[(0 * kFI + r) * kFM + q0 + o] = a0;
+      sh[(1 * kFI + r) * kFM + q0 + o] = a1;
+      sh[(2 * kFI + r) * kFM + q0 + o] = a2;
+      sh[(3 * kFI + r) * kFM + q0 + o] = a3;
+      sh[(4 * kFI + r) * kFM + q0 + o] = a4;
+    }
   }
   __syncthreads();
-  const int ly = t / kT, lx = t % kT;
-  const int gy = ty0 + ly, gx = tx0 + lx;
-  float mu_x = 0.f, mu_y = 0.f, exx = 0.f, eyy = 0.f, exy = 0.f;
+  // vertical moments, SSIM and its derivatives on the 42x42 map region:
+  // each item is a column segment of kSeg rows. The maps overwrite the input
+  // window, so every item is computed before any is stored.
+  float ssum = 0.f, lsum = 0.f;
+  constexpr int kV1Items = kFM * kHSeg;  // 294
+  constexpr int kV1PerThread = (kV1Items + 255) / 256;
+  float dm[kV1PerThread][3][kSeg];
 #pragma unroll
-  for (int j = 0; j < 11; ++j) {
-    const float w = c_win[j];
-    mu_x += w * s_h[0][ly + j][lx];
-    mu_y += w * s_h[1][ly + j][lx];
-    exx += w * s_h[2][ly + j][lx];
-    eyy += w * s_h[3][ly + j][lx];
-    exy += w * s_h[4][ly + j][lx];
+  for (int it = 0; it < kV1PerThread; ++it) {
+    const int k = t + it * 256;
+    if (k >= kV1Items) break;
+    const int q = k % kFM, r0 = (k / kFM) * kSeg;
+    float m[5][kSeg];
+#pragma unroll
+    for (int qq = 0; qq < 5; ++qq) {
+      float col[kSeg + 10];
+#pragma unroll
+      for (int i = 0; i < kSeg + 10; ++i) col[i] = sh[(qq * kFI + r0 + i) * kFM + q];
+#pragma unroll
+      for (int o = 0; o < kSeg; ++o) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 11; ++j) acc += c_win[j] * col[o + j];
+        m[qq][o] = acc;
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < kSeg; ++o) {
+      const int r = r0 + o;
+      const int gy = y0 - kR + r, gx = x0 - kR + q;
+      float d_mu = 0.f, d_exx = 0.f, d_exy = 0.f;
+      if (gx >= 0 && gx < W && gy >= 0 && gy < H) {
+        const float mu_x = m[0][o], mu_y = m[1][o], exx = m[2][o], eyy = m[3][o], exy = m[4][o];
+        const float C1 = 0.0001f, C2 = 0.0009f;
+        const float A = 2.f * mu_x * mu_y + C1;
+        const float B = 2.f * (exy - mu_x * mu_y) + C2;
+        const float Cc = mu_x * mu_x + mu_y * mu_y + C1;
+        const float D = (exx - mu_x * mu_x) + (eyy - mu_y * mu_y) + C2;
+        const float inv = 1.0f / (Cc * D);
+        const float ssim = A * B * inv;
+        d_mu = 2.f * mu_y * (B - A) * inv - 2.f * mu_x * ssim * (1.f / Cc - 1.f / D);
+        d_exx = -ssim / D;
+        d_exy = 2.f * A * inv;
+        if (r >= kR && r < kR + kFO && q >= kR && q < kR + kFO) ssum += ssim;  // own pixels
+      }
+      dm[it][0][o] = d_mu;
+      dm[it][1][o] = d_exx;
+      dm[it][2][o] = d_exy;
+    }
   }
-  float ssim = 0.f, l1 = 0.f;
-  if (gx < W && gy < H) {
-    const float C1 = 0.0001f, C2 = 0.0009f;
-    const float A = 2.f * mu_x * mu_y + C1;
-    const float B = 2.f * (exy - mu_x * mu_y) + C2;
-    const float Cc = mu_x * mu_x + mu_y * mu_y + C1;
-    const float D = (exx - mu_x * mu_x) + (eyy - mu_y * mu_y) + C2;
-    const float inv = 1.0f / (Cc * D);
-    ssim = A * B * inv;
-    const float d_mu = 2.f * mu_y * (B - A) * inv - 2.f * mu_x * ssim * (1.f / Cc - 1.f / D);
-    const float d_exx = -ssim / D;
-    const float d_exy = 2.f * A * inv;
-    const size_t pix = (size_t)gy * W + gx;
-    maps[(0 * 3 + c) * P + pix] = d_mu;
-    maps[(1 * 3 + c) * P + pix] = d_exx;
-    maps[(2 * 3 + c) * P + pix] = d_exy;
-    l1 = fabsf(s_x[ly + kR][lx + kR] - s_y[ly + kR][lx + kR]);
+  __syncthreads();  // the input window is dead from here on
+#pragma unroll
+  for (int it = 0; it < kV1PerThread; ++it) {
+    const int k = t + it * 256;
+    if (k >= kV1Items) break;
+    const int q = k % kFM, r0 = (k / kFM) * kSeg;
+#pragma unroll
+    for (int o = 0; o < kSeg; ++o) {
+      mp[(0 * kFM + r0 + o) * (kFM + 1) + q] = dm[it][0][o];
+      mp[(1 * kFM + r0 + o) * (kFM + 1) + q] = dm[it][1][o];
+      mp[(2 * kFM + r0 + o) * (kFM + 1) + q] = dm[it][2][o];
+    }
   }
-  // block partial sums (deterministic per block)
-  float a = ssim, b = l1;
+  __syncthreads();
+  // horizontal convolution of the derivative maps: row segments of 8
+  constexpr int kSeg2 = 8;
+  for (int k = t; k < kFM * (kFO / kSeg2); k += 256) {
+    const int r = k / (kFO / kSeg2), q0 = (k % (kFO / kSeg2)) * kSeg2;
+#pragma unroll
+    for (int qq = 0; qq < 3; ++qq) {
+      float row[kSeg2 + 10];
+#pragma unroll
+      for (int i = 0; i < kSeg2 + 10; ++i) row[i] = mp[(qq * kFM + r) * (kFM + 1) + q0 + i];
+#pragma unroll
+      for (int o = 0; o < kSeg2; ++o) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 11; ++j) acc += c_win[j] * row[o + j];
+        h2[(qq * kFM + r) * kFO + q0 + o] = acc;
+      }
+    }
+  }
+  __syncthreads();
+  // vertical convolution and the image gradient: column segments of 8
+  for (int k = t; k < kFO * (kFO / kSeg2); k += 256) {
+    const int q = k % kFO, r0 = (k / kFO) * kSeg2;
+    float g[3][kSeg2];
+#pragma unroll
+    for (int qq = 0; qq < 3; ++qq) {
+      float col[kSeg2 + 10];
+#pragma unroll
+      for (int i = 0; i < kSeg2 + 10; ++i) col[i] = h2[(qq * kFM + r0 + i) * kFO + q];
+#pragma unroll
+      for (int o = 0; o < kSeg2; ++o) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 11; ++j) acc += c_win[j] * col[o + j];
+        g[qq][o] = acc;
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < kSeg2; ++o) {
+      const int r = r0 + o;
+      const int gy = y0 + r, gx = x0 + q;
+      if (gx >= W || gy >= H) continue;
+      const size_t pix = c * P + (size_t)gy * W + gx;
+      const float xv = x[pix], yv = y[pix];
+      lsum += fabsf(xv - yv);
+      const float sgn = xv > yv ? 1.f : (xv < yv ? -1.f : 0.f);
+      dx[pix] =
+          w_l1_n * sgn - w_ssim_n * (g[0][o] + 2.f * xv * g[1][o] + yv * g[2][o]);
+    }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
+    ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
   }
   if ((t & 31) == 0) {
-    s_red[0][t >> 5] = a;
-    s_red[1][t >> 5] = b;
+    s_red[0][t >> 5] = ssum;
+    s_red[1][t >> 5] = lsum;
   }
   __syncthreads();
   if (t == 0) {
@@ -131,57 +243,6 @@ __global__ void __launch_bounds__(256)
     partials[2 * blk] = sa;
     partials[2 * blk + 1] = sb;
   }
-}
-
-__global__ void __launch_bounds__(256)
-    ssim_bwd_kernel(int W, int H, const float* __restrict__ x, const float* __restrict__ y,
-                    const float* __restrict__ maps, float w_l1_n, float w_ssim_n,
-                    float* __restrict__ dx) {
-  __shared__ float s_m[3][kS][kS + 1];
-  __shared__ float s_h[3][kS][kT + 1];
-  const int tx0 = blockIdx.x * kT, ty0 = blockIdx.y * kT;
-  const int c = blockIdx.z;
-  const size_t P = (size_t)W * H;
-  const int t = threadIdx.x;
-  for (int k = t; k < kS * kS; k += 256) {
-    const int r = k / kS, q = k % kS;
-    const int gy = ty0 - kR + r, gx = tx0 - kR + q;
-    const bool in = gx >= 0 && gx < W && gy >= 0 && gy < H;
-    const size_t pix = (size_t)gy * W + gx;
-#pragma unroll
-    for (int m = 0; m < 3; ++m) s_m[m][r][q] = in ? maps[(m * 3 + c) * P + pix] : 0.0f;
-  }
-  __syncthreads();
-  for (int k = t; k < kS * kT; k += 256) {
-    const int r = k / kT, q = k % kT;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
-#pragma unroll
-    for (int j = 0; j < 11; ++j) {
-      const float w = c_win[j];
-      a0 += w * s_m[0][r][q + j];
-      a1 += w * s_m[1][r][q + j];
-      a2 += w * s_m[2][r][q + j];
-    }
-    s_h[0][r][q] = a0;
-    s_h[1][r][q] = a1;
-    s_h[2][r][q] = a2;
-  }
-  __syncthreads();
-  const int ly = t / kT, lx = t % kT;
-  const int gy = ty0 + ly, gx = tx0 + lx;
-  if (gx >= W || gy >= H) return;
-  float g0 = 0.f, g1 = 0.f, g2 = 0.f;
-#pragma unroll
-  for (int j = 0; j < 11; ++j) {
-    const float w = c_win[j];
-    g0 += w * s_h[0][ly + j][lx];
-    g1 += w * s_h[1][ly + j][lx];
-    g2 += w * s_h[2][ly + j][lx];
-  }
-  const size_t pix = (size_t)gy * W + gx;
-  const float xv = x[c * P + pix], yv = y[c * P + pix];
-  const float sgn = xv > yv ? 1.f : (xv < yv ? -1.f : 0.f);
-  dx[c * P + pix] = w_l1_n * sgn - w_ssim_n * (g0 + 2.f * xv * g1 + yv * g2);
 }
 
 __global__ void loss_finalize_kernel(const float* __restrict__ partials, int nblk, float w_l1,
@@ -457,9 +518,8 @@ int fgs_activate_params(int64_t n, const float* params_flat, float* opacities, f
 }
 
 size_t fgs_loss_scratch_bytes(int32_t width, int32_t height) {
-  const size_t P = (size_t)width * height;
-  const size_t blocks = (size_t)((width + kT - 1) / kT) * ((height + kT - 1) / kT) * 3;
-  return (9 * P + 2 * blocks) * sizeof(float);
+  const size_t blocks = (size_t)((width + kFO - 1) / kFO) * ((height + kFO - 1) / kFO) * 3;
+  return (2 * blocks + 64) * sizeof(float);
 }
 
 int fgs_l1_dssim_loss(int32_t width, int32_t height, const float* image, const float* target,
@@ -471,15 +531,16 @@ int fgs_l1_dssim_loss(int32_t width, int32_t height, const float* image, const f
   if (st) return st;
   cudaStream_t s = (cudaStream_t)stream;
   const size_t P = (size_t)width * height;
-  float* maps = (float*)scratch;
-  float* partials = maps + 9 * P;
-  dim3 grid((width + kT - 1) / kT, (height + kT - 1) / kT, 3);
+  float* partials = (float*)scratch;
+  dim3 grid((width + kFO - 1) / kFO, (height + kFO - 1) / kFO, 3);
   const int nblk = (int)(grid.x * grid.y * grid.z);
-  ssim_fwd_kernel<<<grid, 256, 0, s>>>(width, height, image, target, maps, partials);
   const float inv_n = 1.0f / (float)(3 * P);
+  const int smem = kFusedSmemFloats * (int)sizeof(float);
+  static unsigned long long attr_done = 0;
+  smem_attr_once(ssim_fused_kernel, smem, &attr_done);
+  ssim_fused_kernel<<<grid, 256, smem, s>>>(width, height, image, target, w_l1 * inv_n,
+                                            w_ssim * inv_n, dL_dimage, partials);
   loss_finalize_kernel<<<1, 1024, 0, s>>>(partials, nblk, w_l1, w_ssim, inv_n, loss_out);
-  ssim_bwd_kernel<<<grid, 256, 0, s>>>(width, height, image, target, maps, w_l1 * inv_n,
-                                       w_ssim * inv_n, dL_dimage);
   return check_launch("l1_dssim_loss");
 }
 

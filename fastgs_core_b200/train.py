@@ -221,7 +221,7 @@ class Trainer:
 
     # kernels each C entry point launches (memsets are not kernels)
     _KERNELS = {"preprocess": 1, "scan": 3, "duplicate": 1, "tile_prep": 2, "rasterize_forward": 1,
-                "loss": 3, "rasterize_backward": 1, "preprocess_backward_train": 1, "activate": 1,
+                "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1, "activate": 1,
                 "adam": 1}
 
     def _call(self, name, fn, *args):
