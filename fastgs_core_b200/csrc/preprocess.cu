@@ -381,7 +381,7 @@ __device__ __forceinline__ v3 v3add(v3 a, v3 b) { return V3(a.x + b.x, a.y + b.y
 
 template <bool kTrain>
 __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a) {
-  extern __shared__ float s_buf[];  // [2][kPreThreads * S3]: staged sh, then dsh
+  extern __shared__ float s_buf[];  // [kPreThreads * S3]: staged sh, overwritten by dsh
   const fgs_preprocess_params& P = a.p;
   const int base = blockIdx.x * kPreThreads;
   const int i = base + threadIdx.x;
@@ -389,14 +389,14 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
   const int cnt = min(kPreThreads, P.n - base);
   const bool sh_path = !P.use_colors_precomp && S3 > 0;
   float* s_sh = s_buf;
-  float* s_dsh = s_buf + kPreThreads * S3;
+  float* s_dsh = s_buf;  // each thread's gradient row aliases its own sh row
   if (sh_path) {
     stage_floats(s_sh, a.sh + (int64_t)base * S3, (int64_t)cnt * S3);
-    for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) s_dsh[k] = 0.0f;
     __syncthreads();
   }
   int32_t my_radius = 0;
   float4 my_dvs = make_float4(0.f, 0.f, 0.f, 0.f);
+  int n_put = 0;  // leading sh coefficients of this thread's row holding gradients
   if (i < P.n) {
     float dm[3] = {0.f, 0.f, 0.f};
     float ddc[3] = {0.f, 0.f, 0.f};
@@ -524,9 +524,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
     g[3 * (k) + 2] = v_.z;   \
   } while (0)
           const float C1 = kSH_C1;
-          PUT(0, v3s(-C1 * y, dRGB));
-          PUT(1, v3s(C1 * z, dRGB));
-          PUT(2, v3s(-C1 * x, dRGB));
+          const float xx = x * x, yy = y * y, zz = z * z;
+          const float xy = x * y, yz = y * z, xz = x * z;
           v3 dx_ = v3s(-C1, SHC(2));
           v3 dy_ = v3s(-C1, SHC(0));
           v3 dz_ = v3s(C1, SHC(1));
@@ -534,13 +533,6 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
             const float C20 = 1.0925484305920792f, C21 = -1.0925484305920792f,
                         C22 = 0.31539156525252005f, C23 = -1.0925484305920792f,
                         C24 = 0.5462742152960396f;
-            const float xx = x * x, yy = y * y, zz = z * z;
-            const float xy = x * y, yz = y * z, xz = x * z;
-            PUT(3, v3s(C20 * xy, dRGB));
-            PUT(4, v3s(C21 * yz, dRGB));
-            PUT(5, v3s(C22 * (2.0f * zz - xx - yy), dRGB));
-            PUT(6, v3s(C23 * xz, dRGB));
-            PUT(7, v3s(C24 * (xx - yy), dRGB));
             {
               v3 s1 = v3s(C20 * y, SHC(3));
               s1 = v3add(s1, v3s(C22 * 2.f * -x, SHC(5)));
@@ -566,13 +558,6 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
                           C32 = -0.4570457994644658f, C33 = 0.3731763325901154f,
                           C34 = -0.4570457994644658f, C35 = 1.445305721320277f,
                           C36 = -0.5900435899266435f;
-              PUT(8, v3s(C30 * y * (3.f * xx - yy), dRGB));
-              PUT(9, v3s(C31 * xy * z, dRGB));
-              PUT(10, v3s(C32 * y * (4.f * zz - xx - yy), dRGB));
-              PUT(11, v3s(C33 * z * (2.f * zz - 3.f * xx - 3.f * yy), dRGB));
-              PUT(12, v3s(C34 * x * (4.f * zz - xx - yy), dRGB));
-              PUT(13, v3s(C35 * z * (xx - yy), dRGB));
-              PUT(14, v3s(C36 * x * (xx - 3.f * yy), dRGB));
               {
                 v3 s1 = v3sr(v3sr(v3s(C30, SHC(8)), 6.f), xy);
                 s1 = v3add(s1, v3sr(v3s(C31, SHC(9)), yz));
@@ -600,6 +585,39 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
                 s1 = v3add(s1, v3sr(v3sr(v3s(C34, SHC(12)), 8.f), xz));
                 s1 = v3add(s1, v3sr(v3s(C35, SHC(13)), (xx - yy)));
                 dz_ = v3add(dz_, s1);
+              }
+            }
+          }
+          // Every SHC read above precedes the first PUT: the gradient row
+          // overwrites this thread's own staged coefficients in place.
+          {
+            const float C20 = 1.0925484305920792f, C21 = -1.0925484305920792f,
+                        C22 = 0.31539156525252005f, C23 = -1.0925484305920792f,
+                        C24 = 0.5462742152960396f;
+            const float C30 = -0.5900435899266435f, C31 = 2.890611442640554f,
+                        C32 = -0.4570457994644658f, C33 = 0.3731763325901154f,
+                        C34 = -0.4570457994644658f, C35 = 1.445305721320277f,
+                        C36 = -0.5900435899266435f;
+            PUT(0, v3s(-C1 * y, dRGB));
+            PUT(1, v3s(C1 * z, dRGB));
+            PUT(2, v3s(-C1 * x, dRGB));
+            n_put = 3;
+            if (P.degree > 1 && P.max_sh_coeffs >= 8) {
+              PUT(3, v3s(C20 * xy, dRGB));
+              PUT(4, v3s(C21 * yz, dRGB));
+              PUT(5, v3s(C22 * (2.0f * zz - xx - yy), dRGB));
+              PUT(6, v3s(C23 * xz, dRGB));
+              PUT(7, v3s(C24 * (xx - yy), dRGB));
+              n_put = 8;
+              if (P.degree > 2 && P.max_sh_coeffs >= 15) {
+                PUT(8, v3s(C30 * y * (3.f * xx - yy), dRGB));
+                PUT(9, v3s(C31 * xy * z, dRGB));
+                PUT(10, v3s(C32 * y * (4.f * zz - xx - yy), dRGB));
+                PUT(11, v3s(C33 * z * (2.f * zz - 3.f * xx - 3.f * yy), dRGB));
+                PUT(12, v3s(C34 * x * (4.f * zz - xx - yy), dRGB));
+                PUT(13, v3s(C35 * z * (xx - yy), dRGB));
+                PUT(14, v3s(C36 * x * (xx - 3.f * yy), dRGB));
+                n_put = 15;
               }
             }
           }
@@ -715,6 +733,10 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
   }
   float* dsh_dst = kTrain ? a.g_rest : a.dsh;
   if (sh_path) {
+    if (threadIdx.x < cnt) {
+      float* row = s_dsh + threadIdx.x * S3;
+      for (int k = 3 * n_put; k < S3; ++k) row[k] = 0.0f;
+    }
     __syncthreads();
     float* gdst = dsh_dst + (int64_t)base * S3;
     if (kTrain && a.accumulate) {
@@ -844,7 +866,7 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
   a.dmeans3d = dL_dmeans3d; a.ddc = dL_ddc; a.dsh = dL_dsh; a.dcolors_precomp = dL_dcolors_precomp;
   a.dopac = dL_dopacities; a.dscales = dL_dscales; a.dquats = dL_dquats; a.dvs_in = dL_dviewspace_in;
   const bool sh_path = !p->use_colors_precomp && p->max_sh_coeffs > 0;
-  const size_t smem = sh_path ? 2 * (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
+  const size_t smem = sh_path ? (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
   static unsigned long long attr_done = 0;
   if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<false>, (int)smem, &attr_done);
   const int blocks = (p->n + kPreThreads - 1) / kPreThreads;
@@ -893,7 +915,7 @@ int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* m
   a.st_denom = stats + 2 * n;
   a.st_max_radii = stats + 3 * n;
   a.accumulate = accumulate;
-  const size_t smem = 2 * (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float);
+  const size_t smem = (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float);
   static unsigned long long attr_done = 0;
   if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<true>, (int)smem, &attr_done);
   const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
