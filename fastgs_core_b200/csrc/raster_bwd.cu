@@ -75,42 +75,52 @@ __device__ __forceinline__ void bwd_splat_rows(float y, float a, float b, float 
   hi = min(FGS_BLOCK, (int)floorf(yl + dymax));
 }
 
-// Sum p[0..15] across the warp so that lanes 2k and 2k+1 hold sum_k.
-__device__ __forceinline__ float warp_transpose_sum16(float (&p)[16], int lane) {
+// Sum p[0..10] across the warp in 13 shuffles (a transposed butterfly: at each
+// level a lane pair splits the values it still holds, each half keeping one
+// part and adding the partner's copy of it). Returns the full sum of slot
+// `slot` (lanes that end with no slot get slot = -1). Level by level the lane
+// bits select: bit 4 -> slots 0-5 / 6-10, bit 3 -> positions 0-2 / 3-5,
+// bit 2 -> positions 0-1 / 2, bit 1 -> the position within that, bit 0 -> the
+// final pairwise sum.
+__device__ __forceinline__ float warp_transpose_sum11(const float (&p)[kSlots], int lane, int& slot) {
+  float q[6];
   {
     const bool hi = lane & 16;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float send = hi ? p[k] : p[k + 8];
-      const float keep = hi ? p[k + 8] : p[k];
-      p[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    for (int i = 0; i < 6; ++i) {
+      const float up = (6 + i < kSlots) ? p[6 + i] : 0.0f;
+      const float send = hi ? p[i] : up;
+      const float keep = hi ? up : p[i];
+      q[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
   }
+  float r[3];
   {
     const bool hi = lane & 8;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float send = hi ? p[k] : p[k + 4];
-      const float keep = hi ? p[k + 4] : p[k];
-      p[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    for (int i = 0; i < 3; ++i) {
+      const float send = hi ? q[i] : q[3 + i];
+      const float keep = hi ? q[3 + i] : q[i];
+      r[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
     }
   }
+  float t0, t1;
   {
     const bool hi = lane & 4;
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float send = hi ? p[k] : p[k + 2];
-      const float keep = hi ? p[k + 2] : p[k];
-      p[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
+    t0 = (hi ? r[2] : r[0]) + __shfl_xor_sync(0xffffffffu, hi ? r[0] : r[2], 4);
+    t1 = (hi ? 0.0f : r[1]) + __shfl_xor_sync(0xffffffffu, r[1], 4);
   }
+  float w;
   {
     const bool hi = lane & 2;
-    const float send = hi ? p[0] : p[1];
-    const float keep = hi ? p[1] : p[0];
-    p[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    w = (hi ? t1 : t0) + __shfl_xor_sync(0xffffffffu, hi ? t0 : t1, 2);
   }
-  return p[0] + __shfl_xor_sync(0xffffffffu, p[0], 1);
+  w += __shfl_xor_sync(0xffffffffu, w, 1);
+  const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1, b1 = (lane >> 1) & 1;
+  const int pos = 3 * b3 + (b2 ? 2 + b1 : b1);
+  slot = ((lane & 1) || (b2 && b1)) ? -1 : 6 * b4 + pos;
+  if (slot >= kSlots) slot = -1;
+  return w;
 }
 
 constexpr int kChunk = 256;  // splats (8 buckets) staged per CTA pass
@@ -205,7 +215,11 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
       if (__float_as_int(r2.w) < wrow || __float_as_int(r2.z) > wrow + kWarpRows - 1) continue;
       const float4 r0 = s_r0[j];
       const float4 r1 = s_r1[j];
-      bool v[PX];
+      // Branch-free per pair: every lane evaluates the exponential (on 0 for
+      // pairs that fail the exponent test, whose result is discarded), and an
+      // invalid pair enters the gradient arithmetic with alpha = 0 and G = 0, so
+      // it leaves T and the remaining-colour dot unchanged and adds zeros.
+      bool v[PX], vg[PX];
       float dx[PX], dy[PX], G[PX], oG[PX], alpha[PX];
       bool any = false;
 #pragma unroll
@@ -214,66 +228,63 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
         dy[k] = r0.y - pfy[k];
         const float power = splat_power(r0.z, r0.w, r1.x, dx[k], dy[k]);
         // same decisions as the forward pass (NaN exponents included)
-        v[k] = (s < last[k]) && !(power > 0.0f) && !(power <= r2.y);
-        G[k] = oG[k] = alpha[k] = 0.f;
-        if (v[k]) {
-          G[k] = fgs_expf_neg(power);
-          oG[k] = __fmul_rn(r1.y, G[k]);
-          alpha[k] = fmin_t(0.99f, oG[k]);
-          v[k] = alpha[k] >= 1.0f / 255.0f;
-        }
+        const bool pre = (s < last[k]) && !(power > 0.0f) && !(power <= r2.y);
+        G[k] = fgs_expf_neg(pre ? power : 0.0f);
+        oG[k] = __fmul_rn(r1.y, G[k]);
+        alpha[k] = fmin_t(0.99f, oG[k]);
+        v[k] = pre && alpha[k] >= 1.0f / 255.0f;
+        vg[k] = v[k] && !(oG[k] > 0.99f);
         any |= v[k];
       }
       if (__ballot_sync(0xffffffffu, any) == 0u) continue;  // warp-uniform
-      float p[16];
+      float p[kSlots];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) p[q] = 0.0f;
+      for (int q = 0; q < kSlots; ++q) p[q] = 0.0f;
       const float c0c = r1.z, c1c = r1.w, c2c = r2.x;
 #pragma unroll
       for (int k = 0; k < PX; ++k) {
-        if (!v[k]) continue;
-        const float wgt = alpha[k] * T[k];
-        const float rec = __fdividef(1.0f, 1.0f - alpha[k]);
+        const float al = v[k] ? alpha[k] : 0.0f;
+        const float wgt = al * T[k];
+        const float rec = __fdividef(1.0f, 1.0f - al);
         const float cdot = c0c * d0[k] + c1c * d1[k] + c2c * d2[k];
         adot[k] += wgt * cdot;  // remaining colour after this splat, dotted with dL/dpix
         const float dL_dalpha = T[k] * cdot + rec * (adot[k] - tfbg[k]);
-        T[k] *= (1.0f - alpha[k]);
+        T[k] *= (1.0f - al);
         p[kR] += wgt * d0[k];
         p[kG] += wgt * d1[k];
         p[kB] += wgt * d2[k];
-        if (!(oG[k] > 0.99f)) {
-          const float u = r1.y * dL_dalpha * G[k];  // dL/dG * G
-          const float tmp_x = -u * (r0.z * dx[k] + r0.w * dy[k]) * hw;
-          const float tmp_y = -u * (r1.x * dy[k] + r0.w * dx[k]) * hh;
-          p[kMx] += tmp_x;
-          p[kMy] += tmp_y;
-          p[kMxAbs] += fabsf(tmp_x);
-          p[kMyAbs] += fabsf(tmp_y);
-          const float qq = -0.5f * u;
-          const float qdx = qq * dx[k];
-          p[kCx] += qdx * dx[k];
-          p[kCy] += qdx * dy[k];
-          p[kCw] += qq * dy[k] * dy[k];
-          p[kOp] += G[k] * dL_dalpha;
-        }
+        // dL/dG * G; the constant factors (-W/2, -H/2, -1/2) are applied at the flush
+        const float u = (vg[k] ? oG[k] : 0.0f) * dL_dalpha;
+        const float tmp_x = u * (r0.z * dx[k] + r0.w * dy[k]);
+        const float tmp_y = u * (r1.x * dy[k] + r0.w * dx[k]);
+        p[kMx] += tmp_x;
+        p[kMy] += tmp_y;
+        p[kMxAbs] += fabsf(tmp_x);
+        p[kMyAbs] += fabsf(tmp_y);
+        const float udx = u * dx[k];
+        p[kCx] += udx * dx[k];
+        p[kCy] += udx * dy[k];
+        p[kCw] += u * dy[k] * dy[k];
+        p[kOp] += (vg[k] ? G[k] : 0.0f) * dL_dalpha;
       }
-      const float tot = warp_transpose_sum16(p, lane);
-      const int slot = lane >> 1;
-      if (!(lane & 1) && slot < kSlots) atomicAdd(&s_acc[j][slot], tot);
+      int slot;
+      const float tot = warp_transpose_sum11(p, lane, slot);
+      if (slot >= 0) atomicAdd(&s_acc[j][slot], tot);
     }
     __syncthreads();
     for (int q = lr; q < cn; q += kThreads) {
       const size_t g = s_id[q];
       const float* vv = s_acc[q];
-      atomicAdd(a.dmeans2d + 2 * g, vv[kMx]);
-      atomicAdd(a.dmeans2d + 2 * g + 1, vv[kMy]);
-      atomicAdd(a.dviewspace + 4 * g, vv[kMx]);
-      atomicAdd(a.dviewspace + 4 * g + 1, vv[kMy]);
-      atomicAdd(a.dviewspace + 4 * g + 2, vv[kMxAbs]);
-      atomicAdd(a.dviewspace + 4 * g + 3, vv[kMyAbs]);
-      atomicAdd(a.dconic + 4 * g, vv[kCx]);
-      atomicAdd(a.dconic + 4 * g + 1, vv[kCy]);
-      atomicAdd(a.dconic + 4 * g + 2, vv[kCw]);
+      const float mx = -hw * vv[kMx], my = -hh * vv[kMy];
+      atomicAdd(a.dmeans2d + 2 * g, mx);
+      atomicAdd(a.dmeans2d + 2 * g + 1, my);
+      atomicAdd(a.dviewspace + 4 * g, mx);
+      atomicAdd(a.dviewspace + 4 * g + 1, my);
+      atomicAdd(a.dviewspace + 4 * g + 2, hw * vv[kMxAbs]);
+      atomicAdd(a.dviewspace + 4 * g + 3, hh * vv[kMyAbs]);
+      atomicAdd(a.dconic + 4 * g, -0.5f * vv[kCx]);
+      atomicAdd(a.dconic + 4 * g + 1, -0.5f * vv[kCy]);
+      atomicAdd(a.dconic + 4 * g + 2, -0.5f * vv[kCw]);
       atomicAdd(a.dconic + 4 * g + 3, vv[kOp]);
       atomicAdd(a.dcolors + 3 * g, vv[kR]);
       atomicAdd(a.dcolors + 3 * g + 1, vv[kG]);
