@@ -1,20 +1,22 @@
 // Tile rasterizer backward on sm_100a (fastgs_core/metal/fastgs_rasterize_backward.metal:24-278).
 //
 // Same gradients as the reference's per-bucket kernel, organised pixel-
-// parallel: one CTA per 16x16 tile, two pixels per thread. The CTA stages the
-// records of up to 256 splats (8 buckets) at a time; each warp (four pixel
-// rows) then walks them front to back on its own, restarting each bucket from
-// the pixel's forward sample (transmittance T and the colour accumulated
-// before the bucket, kept as its dot product with dL/dpixel, which is all the
-// alpha gradient needs). Per splat, a warp skips the splat outright when the
-// splat's opacity-aware row extent misses its rows, or when no lane's pair
-// passes the alpha test (ballot); otherwise the eleven per-pair partials are
-// summed across the warp with a five-level transposed butterfly (lane 2k ends
-// with value k) and added to shared-memory accumulators; after the chunk, one
-// global atomic per splat and output element. Compared with one warp per bucket
-// (the reference's layout), this evaluates the same pairs but skips whole
-// warp-splat blocks that cannot contribute and avoids the 31-step pipeline
-// fill of the lane-to-lane state shift.
+// parallel with two pixels per thread. Work is split by buckets, not tiles: a
+// CTA takes 8 consecutive buckets (256 splats) of the global bucket list, which
+// bounds every CTA's work whatever the tile's splat count; a bucket is a valid
+// starting point because the forward pass sampled each pixel's transmittance
+// and accumulated colour there. Each warp (four pixel rows) walks the staged
+// splats front to back on its own, restarting at each bucket from the forward
+// sample (the accumulated colour is kept as its dot product with dL/dpixel,
+// which is all the alpha gradient needs). Per splat, a warp skips the splat
+// outright when the splat's opacity-aware row extent misses its rows, or when
+// no lane's pair passes the alpha test (ballot); otherwise the eleven per-pair
+// partials are summed across the warp with a transposed butterfly (13
+// shuffles) and added to shared-memory accumulators; at the end, one global
+// atomic per splat and output element. Compared with one warp per bucket (the
+// reference's layout), this evaluates the same pairs but skips whole warp-splat
+// blocks that cannot contribute and avoids the 31-step pipeline fill of the
+// lane-to-lane state shift.
 //
 // Compiled with multiply-add contraction: gradient arithmetic may fuse. The
 // per-pair decisions must match the forward pass exactly, so the exponent
@@ -123,93 +125,142 @@ __device__ __forceinline__ float warp_transpose_sum11(const float (&p)[kSlots], 
   return w;
 }
 
-constexpr int kChunk = 256;  // splats (8 buckets) staged per CTA pass
+constexpr int kChunk = 256;  // splats (8 buckets) staged per CTA
 constexpr int kBwdPixelsPerThread = 2;
 
+// One CTA per group of kGroupBuckets consecutive buckets of the global bucket
+// list (kChunk splats at most), so that every CTA carries the same bounded work
+// whatever the per-tile splat counts (tiles of this workload range from a few
+// splats to thousands). A group may cover the tail of one tile and the head of
+// the next: the warps walk it bucket by bucket, loading a tile's pixel state
+// when the tile changes and the forward sample (T, accumulated colour) at every
+// bucket start, which is what makes a bucket a valid starting point.
+//
 // PX pixels per thread: a warp covers 2*PX consecutive pixel rows of the tile
 // (lane l: column l % 16, rows base + l / 16 + 2k), so the cross-lane reduction
 // of a splat's partials is shared by 32*PX pixels.
+constexpr int kGroupBuckets = kChunk / 32;
+
 template <int PX>
 __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
   constexpr int kThreads = kTilePx / PX;
   constexpr int kWarpRows = 2 * PX;
-  // splat records of the current chunk
+  // splat records of the group
   __shared__ float4 s_r0[kChunk];  // x, y, conic.a, conic.b
   __shared__ float4 s_r1[kChunk];  // conic.c, opacity, r, g
   __shared__ float4 s_r2[kChunk];  // b, exponent cut, rows lo / hi (int bits)
   __shared__ uint32_t s_id[kChunk];
   __shared__ float s_acc[kChunk][kSlots];
+  __shared__ int s_btile[kGroupBuckets];   // tile of each bucket
+  __shared__ int s_blocal[kGroupBuckets];  // bucket index within its tile
+  __shared__ int s_bcount[kGroupBuckets];  // splats of the bucket to walk (0: skip)
+  __shared__ uint32_t s_bfirst[kGroupBuckets];  // key index of the bucket's first splat
 
-  const int tile = blockIdx.x;
   const int lr = threadIdx.x, lane = lr & 31;
   const int wrow = (lr >> 5) * kWarpRows;
-  const uint2 range = a.ranges[tile];
-  const int nsplat = (int)(range.y - range.x);
-  // buckets at or past max_contrib have no contributing pixel (reference:
-  // fastgs_rasterize_backward.metal:72-74)
-  const int nact = min(nsplat, (int)((a.max_contrib[tile] + 31u) / 32u) * 32);
-  if (nact <= 0) return;
-  const uint32_t bbm0 = (tile == 0) ? 0u : a.bucket_offsets[tile - 1];
-  const int tx = tile % a.gx, ty = tile / a.gx;
-  const int pminx = tx * FGS_BLOCK, pminy = ty * FGS_BLOCK;
-  const size_t P = (size_t)a.W * a.H;
-  const float hw = 0.5f * (float)a.W, hh = 0.5f * (float)a.H;
-
-  int lpix[PX];  // pixel index within the tile
-  float pfx[PX], pfy[PX], d0[PX], d1[PX], d2[PX], tfbg[PX], pcd[PX], T[PX], adot[PX];
-  int last[PX];
-#pragma unroll
-  for (int k = 0; k < PX; ++k) {
-    const int row = wrow + (lane >> 4) + 2 * k;
-    lpix[k] = row * FGS_BLOCK + (lane & 15);
-    const int px = pminx + (lane & 15), py = pminy + row;
-    pfx[k] = (float)px;
-    pfy[k] = (float)py;
-    d0[k] = d1[k] = d2[k] = tfbg[k] = pcd[k] = T[k] = adot[k] = 0.f;
-    last[k] = 0;
-    if (px < a.W && py < a.H) {
-      const size_t pix = (size_t)py * a.W + px;
-      d0[k] = a.dL_dout[pix];
-      d1[k] = a.dL_dout[P + pix];
-      d2[k] = a.dL_dout[2 * P + pix];
-      tfbg[k] = a.final_t[pix] * (a.bg[0] * d0[k] + a.bg[1] * d1[k] + a.bg[2] * d2[k]);
-      // final colour . dL/dpix: the per-bucket remaining-colour dot starts from
-      // (sampled colour - final colour) . dL/dpix
-      pcd[k] = a.pixel_colors[pix] * d0[k] + a.pixel_colors[P + pix] * d1[k] +
-               a.pixel_colors[2 * P + pix] * d2[k];
-      last[k] = (int)a.n_contrib[pix];
+  const int64_t gb0 = (int64_t)blockIdx.x * kGroupBuckets;
+  if (lr < kGroupBuckets) {
+    const int64_t b = gb0 + lr;
+    int tile = -1, local = 0, count = 0;
+    uint32_t first = 0;
+    if (b < a.bucket_sum) {
+      const uint32_t t = a.bucket_to_tile[b];
+      if (t < (uint32_t)a.num_tiles) {
+        tile = (int)t;
+        const uint32_t bbm0 = (t == 0) ? 0u : a.bucket_offsets[t - 1];
+        const uint2 range = a.ranges[t];
+        const int nsplat = (int)(range.y - range.x);
+        // splats at or past max_contrib touch no pixel (reference:
+        // fastgs_rasterize_backward.metal:72-74)
+        const int nact = min(nsplat, (int)((a.max_contrib[t] + 31u) / 32u) * 32);
+        local = (int)((uint32_t)b - bbm0);
+        count = max(0, min(32, nact - 32 * local));
+        first = range.x + 32u * (uint32_t)local;
+      }
     }
+    s_btile[lr] = count > 0 ? tile : -1;
+    s_blocal[lr] = local;
+    s_bcount[lr] = count;
+    s_bfirst[lr] = first;
   }
-
-  for (int c0 = 0; c0 < nact; c0 += kChunk) {
-    const int cn = min(kChunk, nact - c0);
-    __syncthreads();  // previous chunk flushed
-    for (int q = lr; q < cn; q += kThreads) {
-      const uint32_t g = a.point_list[range.x + c0 + q];
+  __syncthreads();
+  {
+    int total = 0;
+#pragma unroll
+    for (int i = 0; i < kGroupBuckets; ++i) total += s_bcount[i];
+    if (total == 0) return;  // uniform: no barrier follows for this CTA
+  }
+  for (int q = lr; q < kChunk; q += kThreads) {
+    const int bi = q >> 5;
+    uint32_t g = 0xffffffffu;
+    if ((q & 31) < s_bcount[bi]) {
+      const int t = s_btile[bi];
+      g = a.point_list[s_bfirst[bi] + (q & 31)];
       const float2 xy = a.means2d[g];
       const float4 co = a.conic[g];
       int rlo, rhi;
-      bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, pminy, rlo, rhi);
+      bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, (t / a.gx) * FGS_BLOCK, rlo, rhi);
       s_r0[q] = make_float4(xy.x, xy.y, co.x, co.y);
       s_r1[q] = make_float4(co.z, co.w, a.colors[3 * (size_t)g], a.colors[3 * (size_t)g + 1]);
       s_r2[q] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), __int_as_float(rlo),
                             __int_as_float(rhi));
-      s_id[q] = g;
     }
-    for (int k = lr; k < kChunk * kSlots; k += kThreads) (&s_acc[0][0])[k] = 0.0f;
-    __syncthreads();
-    for (int j = 0; j < cn; ++j) {
-      const int s = c0 + j;
-      if ((s & 31) == 0) {
-        // bucket start: the forward sample of each pixel
-        const size_t bucket = (size_t)bbm0 + (size_t)(s >> 5);
+    s_id[q] = g;
+  }
+  for (int k = lr; k < kChunk * kSlots; k += kThreads) (&s_acc[0][0])[k] = 0.0f;
+  __syncthreads();
+
+  const size_t P = (size_t)a.W * a.H;
+  const float hw = 0.5f * (float)a.W, hh = 0.5f * (float)a.H;
+  int lpix[PX];  // pixel index within the tile
+  float pfx[PX], pfy[PX], d0[PX], d1[PX], d2[PX], tfbg[PX], pcd[PX], T[PX], adot[PX];
+  int last[PX];
+  int cur_tile = -1;
+  for (int bi = 0; bi < kGroupBuckets; ++bi) {
+    const int cnt = s_bcount[bi];
+    if (cnt == 0) continue;  // uniform
+    const int tile = s_btile[bi];
+    if (tile != cur_tile) {
+      // the pixel state of a new tile
+      cur_tile = tile;
+      const int pminx = (tile % a.gx) * FGS_BLOCK, pminy = (tile / a.gx) * FGS_BLOCK;
 #pragma unroll
-        for (int k = 0; k < PX; ++k) {
-          T[k] = a.sampled_t[bucket * kTilePx + lpix[k]];
-          const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lpix[k];
-          adot[k] = sar[0] * d0[k] + sar[kTilePx] * d1[k] + sar[2 * kTilePx] * d2[k] - pcd[k];
+      for (int k = 0; k < PX; ++k) {
+        const int row = wrow + (lane >> 4) + 2 * k;
+        lpix[k] = row * FGS_BLOCK + (lane & 15);
+        const int px = pminx + (lane & 15), py = pminy + row;
+        pfx[k] = (float)px;
+        pfy[k] = (float)py;
+        d0[k] = d1[k] = d2[k] = tfbg[k] = pcd[k] = 0.f;
+        last[k] = 0;
+        if (px < a.W && py < a.H) {
+          const size_t pix = (size_t)py * a.W + px;
+          d0[k] = a.dL_dout[pix];
+          d1[k] = a.dL_dout[P + pix];
+          d2[k] = a.dL_dout[2 * P + pix];
+          tfbg[k] = a.final_t[pix] * (a.bg[0] * d0[k] + a.bg[1] * d1[k] + a.bg[2] * d2[k]);
+          // final colour . dL/dpix: the per-bucket remaining-colour dot starts
+          // from (sampled colour - final colour) . dL/dpix
+          pcd[k] = a.pixel_colors[pix] * d0[k] + a.pixel_colors[P + pix] * d1[k] +
+                   a.pixel_colors[2 * P + pix] * d2[k];
+          last[k] = (int)a.n_contrib[pix];
         }
       }
+    }
+    {
+      // bucket start: the forward sample of each pixel
+      const size_t bucket = (size_t)(gb0 + bi);
+#pragma unroll
+      for (int k = 0; k < PX; ++k) {
+        T[k] = a.sampled_t[bucket * kTilePx + lpix[k]];
+        const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lpix[k];
+        adot[k] = sar[0] * d0[k] + sar[kTilePx] * d1[k] + sar[2 * kTilePx] * d2[k] - pcd[k];
+      }
+    }
+    const int sbase = 32 * s_blocal[bi];
+    for (int jj = 0; jj < cnt; ++jj) {
+      const int j = 32 * bi + jj;  // staged record
+      const int s = sbase + jj;    // splat index within the tile
       const float4 r2 = s_r2[j];
       // warp-uniform: the splat cannot reach this warp's rows
       if (__float_as_int(r2.w) < wrow || __float_as_int(r2.z) > wrow + kWarpRows - 1) continue;
@@ -271,25 +322,27 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
       const float tot = warp_transpose_sum11(p, lane, slot);
       if (slot >= 0) atomicAdd(&s_acc[j][slot], tot);
     }
-    __syncthreads();
-    for (int q = lr; q < cn; q += kThreads) {
-      const size_t g = s_id[q];
-      const float* vv = s_acc[q];
-      const float mx = -hw * vv[kMx], my = -hh * vv[kMy];
-      atomicAdd(a.dmeans2d + 2 * g, mx);
-      atomicAdd(a.dmeans2d + 2 * g + 1, my);
-      atomicAdd(a.dviewspace + 4 * g, mx);
-      atomicAdd(a.dviewspace + 4 * g + 1, my);
-      atomicAdd(a.dviewspace + 4 * g + 2, hw * vv[kMxAbs]);
-      atomicAdd(a.dviewspace + 4 * g + 3, hh * vv[kMyAbs]);
-      atomicAdd(a.dconic + 4 * g, -0.5f * vv[kCx]);
-      atomicAdd(a.dconic + 4 * g + 1, -0.5f * vv[kCy]);
-      atomicAdd(a.dconic + 4 * g + 2, -0.5f * vv[kCw]);
-      atomicAdd(a.dconic + 4 * g + 3, vv[kOp]);
-      atomicAdd(a.dcolors + 3 * g, vv[kR]);
-      atomicAdd(a.dcolors + 3 * g + 1, vv[kG]);
-      atomicAdd(a.dcolors + 3 * g + 2, vv[kB]);
-    }
+  }
+  __syncthreads();
+  for (int q = lr; q < kChunk; q += kThreads) {
+    const uint32_t gid = s_id[q];
+    if (gid == 0xffffffffu) continue;
+    const size_t g = gid;
+    const float* vv = s_acc[q];
+    const float mx = -hw * vv[kMx], my = -hh * vv[kMy];
+    atomicAdd(a.dmeans2d + 2 * g, mx);
+    atomicAdd(a.dmeans2d + 2 * g + 1, my);
+    atomicAdd(a.dviewspace + 4 * g, mx);
+    atomicAdd(a.dviewspace + 4 * g + 1, my);
+    atomicAdd(a.dviewspace + 4 * g + 2, hw * vv[kMxAbs]);
+    atomicAdd(a.dviewspace + 4 * g + 3, hh * vv[kMyAbs]);
+    atomicAdd(a.dconic + 4 * g, -0.5f * vv[kCx]);
+    atomicAdd(a.dconic + 4 * g + 1, -0.5f * vv[kCy]);
+    atomicAdd(a.dconic + 4 * g + 2, -0.5f * vv[kCw]);
+    atomicAdd(a.dconic + 4 * g + 3, vv[kOp]);
+    atomicAdd(a.dcolors + 3 * g, vv[kR]);
+    atomicAdd(a.dcolors + 3 * g + 1, vv[kG]);
+    atomicAdd(a.dcolors + 3 * g + 2, vv[kB]);
   }
 }
 
@@ -347,7 +400,9 @@ int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
   a.dviewspace = dL_dviewspace;
   // two pixels per thread (measured on config 3: 1.68 ms vs 1.91 ms with one
   // and 1.98 ms with four, where occupancy drops)
-  raster_bwd_kernel<kBwdPixelsPerThread><<<p->num_tiles, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
+  const int64_t groups = (p->bucket_sum + kGroupBuckets - 1) / kGroupBuckets;
+  FGS_CHECK_ARG(groups <= 0x7fffffff, "too many buckets");
+  raster_bwd_kernel<kBwdPixelsPerThread><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
   return check_launch("rasterize_backward");
 }
 
