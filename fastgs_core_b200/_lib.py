@@ -29,7 +29,8 @@ class PreprocessParams(C.Structure):
 
 class RasterParams(C.Structure):
     _fields_ = [("image_width", _i32), ("image_height", _i32), ("num_tiles", _i32),
-                ("bucket_sum", _i64), ("num_gaussians", _i32), ("get_flag", _i32)]
+                ("bucket_sum", _i64), ("num_gaussians", _i32), ("get_flag", _i32),
+                ("tile_order", _p)]
 
 
 # name -> (restype, argtypes)
@@ -44,6 +45,7 @@ _SIGS = {
     "fgs_sort_pairs": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
     "fgs_sort_pairs_static": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p]),
     "fgs_tile_prep": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _p]),
+    "fgs_tile_order": (C.c_int, [_i32, _p, _p, _p]),
     "fgs_rasterize_forward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 18),
     "fgs_rasterize_backward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 20),
     "fgs_preprocess_backward": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 24),

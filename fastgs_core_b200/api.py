@@ -392,6 +392,10 @@ def _run_rasterize(rp: RasterParams, t: dict, dev) -> dict:
     # written (fastgs_rasterize.metal:67-75); the rest stay at the zero fill
     if B:
         o["bucket_to_tile"][B:].zero_()
+    # heaviest tiles first (same results in any order)
+    order = torch.empty(rp.num_tiles, dtype=torch.uint32, device=dev)
+    check(lib().fgs_tile_order(rp.num_tiles, _p(t["ranges"]), _p(order), _stream(dev)), "tile_order")
+    rp.tile_order = order.data_ptr() if rp.num_tiles else None
     st = lib().fgs_rasterize_forward(
         C.byref(rp), *[_p(t[k]) for k in ("ranges", "point_list", "bucket_offsets", "means2d",
                                           "colors", "conic_opacity", "background", "metric_map")],

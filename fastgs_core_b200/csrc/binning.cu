@@ -257,6 +257,52 @@ __global__ void tile_ranges_kernel(const uint64_t* __restrict__ keys, int64_t n,
   if (g == n - 1 && valid && cur < (uint32_t)num_tiles) ranges[2 * (size_t)cur + 1] = (uint32_t)n;
 }
 
+// one CTA: tiles in descending order of their splat count (counting sort on
+// ceil(count / 16), 256 classes, the last class open-ended). Rendering the
+// heaviest tiles first keeps a few long tiles from finishing alone at the end
+// of a tile-per-CTA launch. The order within a class is unspecified; every
+// tile's results are independent of it.
+constexpr int kOrderClasses = 256;
+__device__ __forceinline__ int tile_order_class(const uint32_t* ranges, int t) {
+  const uint32_t ns = ranges[2 * t + 1] - ranges[2 * t];
+  return (int)min((ns + 15u) / 16u, (uint32_t)(kOrderClasses - 1));
+}
+
+__global__ void __launch_bounds__(1024)
+    tile_order_kernel(const uint32_t* __restrict__ ranges, int num_tiles, uint32_t* __restrict__ order) {
+  __shared__ uint32_t s_hist[kOrderClasses];
+  for (int c = threadIdx.x; c < kOrderClasses; c += blockDim.x) s_hist[c] = 0;
+  __syncthreads();
+  for (int t = threadIdx.x; t < num_tiles; t += blockDim.x) atomicAdd(&s_hist[tile_order_class(ranges, t)], 1u);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // exclusive scan from the heaviest class down: lane l owns classes
+    // 255 - 8l ... 248 - 8l
+    const int lane = threadIdx.x;
+    uint32_t v[8], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      v[k] = s_hist[kOrderClasses - 1 - (8 * lane + k)];
+      sum += v[k];
+    }
+    uint32_t x = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    uint32_t run = x - sum;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      s_hist[kOrderClasses - 1 - (8 * lane + k)] = run;
+      run += v[k];
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < num_tiles; t += blockDim.x)
+    order[atomicAdd(&s_hist[tile_order_class(ranges, t)], 1u)] = (uint32_t)t;
+}
+
 // one CTA: bucket counts, their inclusive scan and the total
 __global__ void __launch_bounds__(1024)
     bucket_count_kernel(const uint32_t* __restrict__ ranges, int num_tiles,
@@ -415,6 +461,14 @@ int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorte
                                                                               num_tiles, ranges);
   bucket_count_kernel<<<1, 1024, 0, s>>>(ranges, num_tiles, bucket_count, bucket_offsets, bucket_sum);
   return check_launch("tile_prep");
+}
+
+int fgs_tile_order(int32_t num_tiles, const uint32_t* ranges, uint32_t* tile_order, void* stream) {
+  FGS_CHECK_ARG(num_tiles >= 0, "num_tiles must be >= 0");
+  if (num_tiles == 0) return FGS_OK;
+  FGS_CHECK_ARG(ranges && tile_order, "missing pointer");
+  tile_order_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(ranges, num_tiles, tile_order);
+  return check_launch("tile_order");
 }
 
 }  // extern "C"

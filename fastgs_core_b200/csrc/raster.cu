@@ -30,6 +30,7 @@ struct FwdArgs {
   const float4* conic;
   const float* bg;
   const int32_t* metric_map;
+  const uint32_t* tile_order;
   uint32_t* bucket_to_tile;
   float* sampled_t;
   float* sampled_ar;
@@ -78,7 +79,7 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
   __shared__ uint32_t s_id[kTile];
   __shared__ uint32_t s_wmax[kThreads / 32];
 
-  const int tile = blockIdx.x;
+  const int tile = a.tile_order ? (int)a.tile_order[blockIdx.x] : (int)blockIdx.x;
   const int lr = threadIdx.x, lane = lr & 31;
   const int tx = tile % a.gx, ty = tile / a.gx;
   const int wrow = (lr >> 5) * kWarpRows;  // this warp's first tile row
@@ -265,6 +266,7 @@ int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
   a.conic = (const float4*)conic_opacity;
   a.bg = background;
   a.metric_map = metric_map;
+  a.tile_order = p->tile_order;
   a.bucket_to_tile = bucket_to_tile;
   a.sampled_t = sampled_t;
   a.sampled_ar = sampled_ar;

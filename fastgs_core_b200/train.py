@@ -220,7 +220,7 @@ class Trainer:
         self.launches = 0
 
     # kernels each C entry point launches (memsets are not kernels)
-    _KERNELS = {"preprocess": 1, "scan": 3, "duplicate": 1, "tile_prep": 2, "rasterize_forward": 1,
+    _KERNELS = {"preprocess": 1, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
                 "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1, "activate": 1,
                 "adam": 1}
 
@@ -357,7 +357,9 @@ class Trainer:
         ncontrib = ws.get("ncontrib", P, torch.uint32)
         maxc = ws.get("maxc", T, torch.uint32)
         pixc = ws.get("pixc", 3 * P, torch.float32)
-        rp = RasterParams(W, H, T, Bmax, n, 0)
+        order = ws.get("tile_order", T, torch.uint32)
+        self._call("tile_order", L.fgs_tile_order, T, _p(ranges), _p(order), st)
+        rp = RasterParams(W, H, T, Bmax, n, 0, order.data_ptr())
         self._call("rasterize_forward", L.fgs_rasterize_forward, C.byref(rp), _p(ranges), _p(svals), _p(boffs), _p(xys), _p(rgb), _p(conic),
             _p(self.background), None, _p(b2t), _p(samp_t), _p(samp_ar), _p(final_t), _p(ncontrib),
             _p(maxc), _p(pixc), _p(img), None, st)

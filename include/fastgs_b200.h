@@ -163,6 +163,14 @@ FGS_API int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_
                   uint32_t* ranges, uint32_t* bucket_count, uint32_t* bucket_offsets,
                   uint64_t* bucket_sum, void* stream);
 
+/* Tiles in descending order of splat count (ranges from fgs_tile_prep) into
+ * tile_order[num_tiles], for fgs_raster_params.tile_order. No reference
+ * counterpart: the reference dispatches tiles in index order
+ * (fastgs_core/fastgs_rasterize.cpp:160-168); this changes only which CTA
+ * renders which tile. */
+FGS_API int fgs_tile_order(int32_t num_tiles, const uint32_t* ranges, uint32_t* tile_order,
+                           void* stream);
+
 /* ---------------------------------------------------------------------------
  * Rasterize forward: one CTA per 16x16 tile, front-to-back alpha blending
  * with early termination, per-32-splat bucket samples for the backward pass.
@@ -179,6 +187,11 @@ typedef struct fgs_raster_params {
   int64_t bucket_sum;
   int32_t num_gaussians;   /* size of metric_count */
   int32_t get_flag;
+  /* Optional [num_tiles] permutation of the tiles: CTA i of the forward pass
+   * renders tile tile_order[i] (fgs_tile_order writes the heaviest-first
+   * order). NULL renders tile i in CTA i. Results do not depend on it. The
+   * backward pass ignores it. */
+  const uint32_t* tile_order;
 } fgs_raster_params;
 
 FGS_API int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,

@@ -180,3 +180,26 @@ def test_sort_full_64bit(cuda_dev):
                           key_bits=64)
     order = np.argsort(keys, kind="stable")
     assert np.array_equal(sk.cpu().numpy(), keys[order]) and np.array_equal(sv.cpu().numpy(), vals[order])
+
+
+def test_tile_order_heaviest_first(cuda_dev):
+    """fgs_tile_order: a permutation of the tiles whose count class
+    ceil(count/16) (capped at 255) never increases along the order."""
+    import ctypes as C
+
+    from fastgs_core_b200._lib import lib
+
+    rng = np.random.default_rng(7)
+    T = 5003
+    counts = rng.integers(0, 5000, T).astype(np.int64)
+    counts[rng.random(T) < 0.3] = 0
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    ranges = np.stack([starts, starts + counts], 1).astype(np.uint32)
+    r = torch.from_numpy(ranges.view(np.int32)).to(cuda_dev)
+    order = torch.empty(T, dtype=torch.int32, device=cuda_dev)
+    assert lib().fgs_tile_order(T, C.c_void_p(r.data_ptr()), C.c_void_p(order.data_ptr()), None) == 0
+    torch.cuda.synchronize()
+    o = order.cpu().numpy()
+    assert np.array_equal(np.sort(o), np.arange(T))
+    cls = np.minimum((counts[o] + 15) // 16, 255)
+    assert np.all(np.diff(cls) <= 0)
