@@ -2,8 +2,8 @@
 //
 // Same gradients as the reference's per-bucket kernel, organised pixel-
 // parallel with two pixels per thread. Work is split by buckets, not tiles: a
-// CTA takes 8 consecutive buckets (256 splats) of the global bucket list, which
-// bounds every CTA's work whatever the tile's splat count; a bucket is a valid
+// CTA takes one bucket (32 splats) of the global bucket list, which bounds
+// every CTA's work whatever the tile's splat count; a bucket is a valid
 // starting point because the forward pass sampled each pixel's transmittance
 // and accumulated colour there. Each warp (four pixel rows) walks the staged
 // splats front to back on its own, restarting at each bucket from the forward
@@ -125,7 +125,9 @@ __device__ __forceinline__ float warp_transpose_sum11(const float (&p)[kSlots], 
   return w;
 }
 
-constexpr int kChunk = 256;  // splats (8 buckets) staged per CTA
+// splats staged per CTA: one bucket (config 3, B200: 1.17 ms; 2 buckets 1.19,
+// 4 buckets 1.24, 8 buckets 1.26)
+constexpr int kChunk = 32;
 constexpr int kBwdPixelsPerThread = 2;
 
 // One CTA per group of kGroupBuckets consecutive buckets of the global bucket
