@@ -396,6 +396,11 @@ def _run_rasterize(rp: RasterParams, t: dict, dev) -> dict:
     order = torch.empty(rp.num_tiles, dtype=torch.uint32, device=dev)
     check(lib().fgs_tile_order(rp.num_tiles, _p(t["ranges"]), _p(order), _stream(dev)), "tile_order")
     rp.tile_order = order.data_ptr() if rp.num_tiles else None
+    # per (bucket, pixel) contributing-splat bits: the backward pass of this
+    # autograd node reads them instead of re-deciding every pair
+    if B:
+        o["contrib_mask"] = torch.empty(B * 256, dtype=torch.uint32, device=dev)
+        rp.contrib_mask = o["contrib_mask"].data_ptr()
     st = lib().fgs_rasterize_forward(
         C.byref(rp), *[_p(t[k]) for k in ("ranges", "point_list", "bucket_offsets", "means2d",
                                           "colors", "conic_opacity", "background", "metric_map")],

@@ -31,6 +31,7 @@ struct FwdArgs {
   const float* bg;
   const int32_t* metric_map;
   const uint32_t* tile_order;
+  uint32_t* contrib_mask;  // optional [bucket][256]: contributing splats of the bucket per pixel
   uint32_t* bucket_to_tile;
   float* sampled_t;
   float* sampled_ar;
@@ -69,7 +70,7 @@ __device__ __forceinline__ void splat_rows(float y, float a, float b, float c, f
 // column l % 16, rows base + l / 16 + 2k), so staged-record reads, the
 // warp-level row culling and the loop are shared by PX pixels. The per-pixel
 // arithmetic is unchanged (bit-identical results).
-template <int PX>
+template <int PX, bool kMask>
 __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
   constexpr int kThreads = kTile / PX;
   constexpr int kWarpRows = 2 * PX;
@@ -145,7 +146,16 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
         ar[2 * kTile] = done[k] ? 0.0f : C2[k];
         any |= !done[k];
       }
-      if (!any) continue;
+      if (!any) {
+        if (kMask) {
+#pragma unroll
+          for (int k = 0; k < PX; ++k) a.contrib_mask[b * kTile + lpix[k]] = 0u;
+        }
+        continue;
+      }
+      uint32_t msk[PX];
+#pragma unroll
+      for (int k = 0; k < PX; ++k) msk[k] = 0u;
       const int kend = min(k0 + 32, cnt);
       for (int j = k0; j < kend; ++j) {
         const float4 r2 = s_r2[j];
@@ -175,7 +185,12 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
           if (count_metric[k]) atomicAdd(a.metric_count + s_id[j], 1);
           T[k] = test_t;
           last[k] = contributor;
+          if (kMask) msk[k] |= 1u << (j & 31);  // k0 is a multiple of 32
         }
+      }
+      if (kMask) {
+#pragma unroll
+        for (int k = 0; k < PX; ++k) a.contrib_mask[b * kTile + lpix[k]] = msk[k];
       }
     }
     processed = batch + cnt;
@@ -191,6 +206,7 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
       ar[0] = 0.0f;
       ar[kTile] = 0.0f;
       ar[2 * kTile] = 0.0f;
+      if (kMask) a.contrib_mask[b * kTile + lpix[k]] = 0u;
     }
   }
   const float bg0 = a.bg[0], bg1 = a.bg[1], bg2 = a.bg[2];
@@ -267,6 +283,7 @@ int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
   a.bg = background;
   a.metric_map = metric_map;
   a.tile_order = p->tile_order;
+  a.contrib_mask = p->contrib_mask;
   a.bucket_to_tile = bucket_to_tile;
   a.sampled_t = sampled_t;
   a.sampled_ar = sampled_ar;
@@ -279,7 +296,10 @@ int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
   if (p->get_flag && p->num_gaussians > 0)
     zero_i32_kernel<<<(p->num_gaussians + 255) / 256, 256, 0, s>>>(metric_count, p->num_gaussians);
   // one pixel per thread (config 3: 0.805 ms; two per thread measured 0.826 ms)
-  raster_fwd_kernel<1><<<p->num_tiles, kTile, 0, s>>>(a);
+  if (a.contrib_mask)
+    raster_fwd_kernel<1, true><<<p->num_tiles, kTile, 0, s>>>(a);
+  else
+    raster_fwd_kernel<1, false><<<p->num_tiles, kTile, 0, s>>>(a);
   return check_launch("rasterize_forward");
 }
 

@@ -47,6 +47,7 @@ struct BwdArgs {
   const uint32_t* n_contrib;
   const uint32_t* max_contrib;
   const float* pixel_colors;
+  const uint32_t* contrib_mask;
   float* dmeans2d;
   float* dcolors;
   float* dconic;
@@ -143,14 +144,14 @@ constexpr int kBwdPixelsPerThread = 2;
 // of a splat's partials is shared by 32*PX pixels.
 constexpr int kGroupBuckets = kChunk / 32;
 
-template <int PX>
+template <int PX, bool kMask>
 __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
   constexpr int kThreads = kTilePx / PX;
   constexpr int kWarpRows = 2 * PX;
   // splat records of the group
   __shared__ float4 s_r0[kChunk];  // x, y, conic.a, conic.b
   __shared__ float4 s_r1[kChunk];  // conic.c, opacity, r, g
-  __shared__ float4 s_r2[kChunk];  // b, exponent cut, rows lo / hi (int bits)
+  __shared__ float4 s_r2[kChunk];  // b, exponent cut, -, warp bands (bits)
   __shared__ uint32_t s_id[kChunk];
   __shared__ float s_acc[kChunk][kSlots];
   __shared__ int s_btile[kGroupBuckets];   // tile of each bucket
@@ -158,8 +159,8 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
   __shared__ int s_bcount[kGroupBuckets];  // splats of the bucket to walk (0: skip)
   __shared__ uint32_t s_bfirst[kGroupBuckets];  // key index of the bucket's first splat
 
-  const int lr = threadIdx.x, lane = lr & 31;
-  const int wrow = (lr >> 5) * kWarpRows;
+  const int lr = threadIdx.x, lane = lr & 31, warp = lr >> 5;
+  const int wrow = warp * kWarpRows;
   const int64_t gb0 = (int64_t)blockIdx.x * kGroupBuckets;
   if (lr < kGroupBuckets) {
     const int64_t b = gb0 + lr;
@@ -200,12 +201,19 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
       g = a.point_list[s_bfirst[bi] + (q & 31)];
       const float2 xy = a.means2d[g];
       const float4 co = a.conic[g];
-      int rlo, rhi;
-      bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, (t / a.gx) * FGS_BLOCK, rlo, rhi);
+      // warps (bands of kWarpRows tile rows) the splat can reach
+      uint32_t bands = (1u << (kThreads / 32)) - 1u;
+      if (!kMask) {
+        int rlo, rhi;
+        bwd_splat_rows(xy.y, co.x, co.y, co.z, co.w, (t / a.gx) * FGS_BLOCK, rlo, rhi);
+        bands = 0u;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w)
+          if (rhi >= w * kWarpRows && rlo <= w * kWarpRows + kWarpRows - 1) bands |= 1u << w;
+      }
       s_r0[q] = make_float4(xy.x, xy.y, co.x, co.y);
       s_r1[q] = make_float4(co.z, co.w, a.colors[3 * (size_t)g], a.colors[3 * (size_t)g + 1]);
-      s_r2[q] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), __int_as_float(rlo),
-                            __int_as_float(rhi));
+      s_r2[q] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), 0.0f, __uint_as_float(bands));
     }
     s_id[q] = g;
   }
@@ -217,6 +225,9 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
   int lpix[PX];  // pixel index within the tile
   float pfx[PX], pfy[PX], d0[PX], d1[PX], d2[PX], tfbg[PX], pcd[PX], T[PX], adot[PX];
   int last[PX];
+  uint32_t msk[PX];  // contrib_mask of the current bucket (kMask)
+#pragma unroll
+  for (int k = 0; k < PX; ++k) msk[k] = 0u;
   int cur_tile = -1;
   for (int bi = 0; bi < kGroupBuckets; ++bi) {
     const int cnt = s_bcount[bi];
@@ -257,39 +268,73 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
         T[k] = a.sampled_t[bucket * kTilePx + lpix[k]];
         const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lpix[k];
         adot[k] = sar[0] * d0[k] + sar[kTilePx] * d1[k] + sar[2 * kTilePx] * d2[k] - pcd[k];
+        if (kMask) msk[k] = a.contrib_mask[bucket * kTilePx + lpix[k]];
       }
     }
+    uint32_t mor = 0u;  // pairs of this thread that contributed, any pixel
+#pragma unroll
+    for (int k = 0; k < PX; ++k) mor |= msk[k];
     const int sbase = 32 * s_blocal[bi];
     for (int jj = 0; jj < cnt; ++jj) {
       const int j = 32 * bi + jj;  // staged record
       const int s = sbase + jj;    // splat index within the tile
-      const float4 r2 = s_r2[j];
-      // warp-uniform: the splat cannot reach this warp's rows
-      if (__float_as_int(r2.w) < wrow || __float_as_int(r2.z) > wrow + kWarpRows - 1) continue;
-      const float4 r0 = s_r0[j];
-      const float4 r1 = s_r1[j];
-      // Branch-free per pair: every lane evaluates the exponential (on 0 for
-      // pairs that fail the exponent test, whose result is discarded), and an
-      // invalid pair enters the gradient arithmetic with alpha = 0 and G = 0, so
-      // it leaves T and the remaining-colour dot unchanged and adds zeros.
       bool v[PX], vg[PX];
       float dx[PX], dy[PX], G[PX], oG[PX], alpha[PX];
-      bool any = false;
+      float4 r0, r1, r2;
+      if constexpr (kMask) {
+        // the forward pass recorded which pairs contributed: skip the splat
+        // when none of this warp's pairs did (warp-uniform), else evaluate
+        // the exponential with the fast intrinsic, except close to the 0.99
+        // clamp, whose side decides whether G receives a gradient and is
+        // therefore taken from the forward pass's exact arithmetic
+        if (__ballot_sync(0xffffffffu, (mor >> jj) & 1u) == 0u) continue;
+        r0 = s_r0[j];
+        r1 = s_r1[j];
+        r2 = s_r2[j];
 #pragma unroll
-      for (int k = 0; k < PX; ++k) {
-        dx[k] = r0.x - pfx[k];
-        dy[k] = r0.y - pfy[k];
-        const float power = splat_power(r0.z, r0.w, r1.x, dx[k], dy[k]);
-        // same decisions as the forward pass (NaN exponents included)
-        const bool pre = (s < last[k]) && !(power > 0.0f) && !(power <= r2.y);
-        G[k] = fgs_expf_neg(pre ? power : 0.0f);
-        oG[k] = __fmul_rn(r1.y, G[k]);
-        alpha[k] = fmin_t(0.99f, oG[k]);
-        v[k] = pre && alpha[k] >= 1.0f / 255.0f;
-        vg[k] = v[k] && !(oG[k] > 0.99f);
-        any |= v[k];
+        for (int k = 0; k < PX; ++k) {
+          v[k] = (msk[k] >> jj) & 1u;
+          dx[k] = r0.x - pfx[k];
+          dy[k] = r0.y - pfy[k];
+          const float power =
+              -0.5f * (r0.z * dx[k] * dx[k] + r1.x * dy[k] * dy[k]) - r0.w * dx[k] * dy[k];
+          G[k] = __expf(power);
+          oG[k] = r1.y * G[k];
+          if (v[k] && fabsf(oG[k] - 0.99f) < 1e-4f) {
+            G[k] = fgs_expf_neg(splat_power(r0.z, r0.w, r1.x, dx[k], dy[k]));
+            oG[k] = __fmul_rn(r1.y, G[k]);
+          }
+          alpha[k] = fmin_t(0.99f, oG[k]);
+          vg[k] = v[k] && !(oG[k] > 0.99f);
+        }
+      } else {
+        r2 = s_r2[j];
+        // warp-uniform: the splat cannot reach this warp's rows
+        if (!((__float_as_uint(r2.w) >> warp) & 1u)) continue;
+        r0 = s_r0[j];
+        r1 = s_r1[j];
+        // Branch-free per pair: every lane evaluates the exponential (on 0
+        // for pairs that fail the exponent test, whose result is discarded),
+        // and an invalid pair enters the gradient arithmetic with alpha = 0
+        // and G = 0, so it leaves T and the remaining-colour dot unchanged
+        // and adds zeros.
+        bool any = false;
+#pragma unroll
+        for (int k = 0; k < PX; ++k) {
+          dx[k] = r0.x - pfx[k];
+          dy[k] = r0.y - pfy[k];
+          const float power = splat_power(r0.z, r0.w, r1.x, dx[k], dy[k]);
+          // same decisions as the forward pass (NaN exponents included)
+          const bool pre = (s < last[k]) && !(power > 0.0f) && !(power <= r2.y);
+          G[k] = fgs_expf_neg(pre ? power : 0.0f);
+          oG[k] = __fmul_rn(r1.y, G[k]);
+          alpha[k] = fmin_t(0.99f, oG[k]);
+          v[k] = pre && alpha[k] >= 1.0f / 255.0f;
+          vg[k] = v[k] && !(oG[k] > 0.99f);
+          any |= v[k];
+        }
+        if (__ballot_sync(0xffffffffu, any) == 0u) continue;  // warp-uniform
       }
-      if (__ballot_sync(0xffffffffu, any) == 0u) continue;  // warp-uniform
       float p[kSlots];
 #pragma unroll
       for (int q = 0; q < kSlots; ++q) p[q] = 0.0f;
@@ -404,7 +449,11 @@ int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
   // and 1.98 ms with four, where occupancy drops)
   const int64_t groups = (p->bucket_sum + kGroupBuckets - 1) / kGroupBuckets;
   FGS_CHECK_ARG(groups <= 0x7fffffff, "too many buckets");
-  raster_bwd_kernel<kBwdPixelsPerThread><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
+  a.contrib_mask = p->contrib_mask;
+  if (a.contrib_mask)
+    raster_bwd_kernel<kBwdPixelsPerThread, true><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
+  else
+    raster_bwd_kernel<kBwdPixelsPerThread, false><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
   return check_launch("rasterize_backward");
 }
 

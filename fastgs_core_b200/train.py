@@ -216,6 +216,8 @@ class Trainer:
         # instrumentation: CUDA events around chosen launches (same stream),
         # and a count of this library's kernel launches
         self.record = set()
+        # forward pass records contributing pairs for the backward pass
+        self.contrib_mask = os.environ.get("FGS_CONTRIB_MASK", "1") != "0"
         self.events: dict[str, list] = {}
         self.launches = 0
 
@@ -359,7 +361,10 @@ class Trainer:
         pixc = ws.get("pixc", 3 * P, torch.float32)
         order = ws.get("tile_order", T, torch.uint32)
         self._call("tile_order", L.fgs_tile_order, T, _p(ranges), _p(order), st)
-        rp = RasterParams(W, H, T, Bmax, n, 0, order.data_ptr())
+        cm_ptr = None
+        if self.contrib_mask:
+            cm_ptr = ws.get("contrib_mask", Bmax * 256, torch.uint32).data_ptr()
+        rp = RasterParams(W, H, T, Bmax, n, 0, order.data_ptr(), cm_ptr)
         self._call("rasterize_forward", L.fgs_rasterize_forward, C.byref(rp), _p(ranges), _p(svals), _p(boffs), _p(xys), _p(rgb), _p(conic),
             _p(self.background), None, _p(b2t), _p(samp_t), _p(samp_ar), _p(final_t), _p(ncontrib),
             _p(maxc), _p(pixc), _p(img), None, st)

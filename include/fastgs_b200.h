@@ -192,6 +192,13 @@ typedef struct fgs_raster_params {
    * order). NULL renders tile i in CTA i. Results do not depend on it. The
    * backward pass ignores it. */
   const uint32_t* tile_order;
+  /* Optional [bucket_sum*256] uint32, bucket-major like sampled_t: bit j of
+   * entry (bucket, pixel) is set when splat j of the bucket contributed to
+   * the pixel. The forward pass writes it when non-NULL; the backward pass,
+   * given the same buffer, takes each pair's contribution from it instead of
+   * re-deciding it (the gradients then use the fast exponential). NULL on
+   * both sides reproduces the reference's recomputation. */
+  uint32_t* contrib_mask;
 } fgs_raster_params;
 
 FGS_API int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,

@@ -203,3 +203,31 @@ def test_tile_order_heaviest_first(cuda_dev):
     assert np.array_equal(np.sort(o), np.arange(T))
     cls = np.minimum((counts[o] + 15) // 16, 255)
     assert np.all(np.diff(cls) <= 0)
+
+
+@pytest.mark.parametrize("case", CASES[1:4], ids=[f"c{c[0]}" for c in CASES[1:4]])
+def test_rasterize_backward_recompute_path(case, cuda_dev):
+    """The functional rasterize_backward (no contribution mask from the
+    forward pass: every pair re-decided, exact exponential) against the
+    oracle's rasterize-level gradients. The autograd path of the chain tests
+    covers the masked variant."""
+    seed, n, deg, W, H, ls, om, bg = case
+    scene, cam = S.small_scene(seed, n, deg, W, H, log_scale_mu=ls, op_mu=om)
+    ins = S.render_inputs(scene, cam, bg)
+    cot = np.random.default_rng(seed + 100).normal(size=(3, W * H)).astype(np.float32)
+    f, b = _oracle(ins, W, H, cam, deg, cot)
+    res, _ = run_chain(ins, W, H, cam.tan_fovx, cam.tan_fovy, deg, cuda_dev)
+    T = res["ranges"].shape[0]
+    fo = {"bucket_to_tile": res["sample_bucket_to_tile"], "sampled_t": res["sample_t"],
+          "sampled_ar": res["sample_ar"], "final_t": res["img_final_t"],
+          "n_contrib": res["img_n_contrib"], "max_contrib": res["img_max_contrib"],
+          "pixel_colors": res["img_pixel_colors"]}
+    fo = {k: torch.from_numpy(np.ascontiguousarray(v)).to(cuda_dev) for k, v in fo.items()}
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda_dev)  # noqa: E731
+    g = fg.rasterize_backward(d(res["ranges"]), d(res["point_list"]), d(res["bucket_offsets"]),
+                              d(res["geom_means2d"]), d(res["geom_rgb"]), d(res["geom_conic_opacity"]),
+                              d(np.asarray(bg, np.float32)), d(cot), fo, W, H, T, res["num_buckets"])
+    for mine, theirs in (("d_means2d", "dmeans2d"), ("d_colors", "dcolors"),
+                         ("d_conic_opacity", "dconic_opacity"), ("d_viewspace_points", "dviewspace_raster")):
+        got = g[mine].cpu().numpy().reshape(b[theirs].shape)
+        assert rel_err(got, b[theirs]) < GRAD_TOL, (mine, rel_err(got, b[theirs]))
