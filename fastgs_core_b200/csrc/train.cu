@@ -283,52 +283,82 @@ struct AdamGroups {
   int count;
 };
 
-__global__ void adam_kernel(int64_t total, float* __restrict__ p, const float* __restrict__ g,
-                            float* __restrict__ m, float* __restrict__ v, AdamGroups grp, float b1,
-                            float b2, float eps, float bc1, float bc2) {
-  const int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t i = 4 * i4;
-  if (i >= total) return;
-  if (i + 4 <= total) {
-    float4 pp = reinterpret_cast<float4*>(p)[i4];
-    const float4 gg = reinterpret_cast<const float4*>(g)[i4];
-    float4 mm = reinterpret_cast<float4*>(m)[i4];
-    float4 vv = reinterpret_cast<float4*>(v)[i4];
-    float* pa = &pp.x;
-    const float* ga = &gg.x;
-    float* ma = &mm.x;
-    float* va = &vv.x;
+__device__ __forceinline__ float adam_lr(const AdamGroups& grp, int64_t idx) {
+  float lr = grp.lr[grp.count - 1];
+  for (int q = 0; q < grp.count; ++q)
+    if (idx < grp.end[q]) {
+      lr = grp.lr[q];
+      break;
+    }
+  return lr;
+}
+
+__device__ __forceinline__ void adam_update4(float4& pp, const float4 gg, float4& mm, float4& vv,
+                                             const AdamGroups& grp, int64_t i, float b1, float b2,
+                                             float eps, float bc1, float bc2) {
+  float* pa = &pp.x;
+  const float* ga = &gg.x;
+  float* ma = &mm.x;
+  float* va = &vv.x;
+  // one group lookup for the four elements unless a group boundary falls inside
+  const float lr0 = adam_lr(grp, i);
+  const bool same = adam_lr(grp, i + 3) == lr0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int64_t idx = i + k;
-      float lr = grp.lr[grp.count - 1];
-      for (int q = 0; q < grp.count; ++q)
-        if (idx < grp.end[q]) {
-          lr = grp.lr[q];
-          break;
-        }
-      ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
-      va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
-      pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
-    }
-    reinterpret_cast<float4*>(p)[i4] = pp;
-    reinterpret_cast<float4*>(m)[i4] = mm;
-    reinterpret_cast<float4*>(v)[i4] = vv;
-  } else {
-    for (int64_t idx = i; idx < total; ++idx) {
-      float lr = grp.lr[grp.count - 1];
-      for (int q = 0; q < grp.count; ++q)
-        if (idx < grp.end[q]) {
-          lr = grp.lr[q];
-          break;
-        }
-      m[idx] = b1 * m[idx] + (1.f - b1) * g[idx];
-      v[idx] = b2 * v[idx] + (1.f - b2) * g[idx] * g[idx];
-      p[idx] -= lr * (m[idx] * bc1) / (sqrtf(v[idx] * bc2) + eps);
-    }
+  for (int k = 0; k < 4; ++k) {
+    const float lr = same ? lr0 : adam_lr(grp, i + k);
+    ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
+    va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
+    pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
   }
 }
 
+// Two float4 per thread per iteration (eight independent 16-byte loads in
+// flight), grid-stride over a grid sized to the SMs; every stream is read
+// once and written once, so loads and stores are marked streaming.
+__global__ void __launch_bounds__(256) adam_kernel(int64_t total, float* __restrict__ p,
+                                                   const float* __restrict__ g, float* __restrict__ m,
+                                                   float* __restrict__ v, AdamGroups grp, float b1,
+                                                   float b2, float eps, float bc1, float bc2) {
+  const int64_t n4 = total / 4;
+  float4* p4 = reinterpret_cast<float4*>(p);
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  float4* m4 = reinterpret_cast<float4*>(m);
+  float4* v4 = reinterpret_cast<float4*>(v);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; j + stride < n4; j += 2 * stride) {
+    const int64_t j2 = j + stride;
+    float4 pa = __ldcs(p4 + j), pb = __ldcs(p4 + j2);
+    const float4 ga = __ldcs(g4 + j), gb = __ldcs(g4 + j2);
+    float4 ma = __ldcs(m4 + j), mb = __ldcs(m4 + j2);
+    float4 va = __ldcs(v4 + j), vb = __ldcs(v4 + j2);
+    adam_update4(pa, ga, ma, va, grp, 4 * j, b1, b2, eps, bc1, bc2);
+    adam_update4(pb, gb, mb, vb, grp, 4 * j2, b1, b2, eps, bc1, bc2);
+    __stcs(p4 + j, pa);
+    __stcs(p4 + j2, pb);
+    __stcs(m4 + j, ma);
+    __stcs(m4 + j2, mb);
+    __stcs(v4 + j, va);
+    __stcs(v4 + j2, vb);
+  }
+  if (j < n4) {
+    float4 pa = __ldcs(p4 + j);
+    const float4 ga = __ldcs(g4 + j);
+    float4 ma = __ldcs(m4 + j), va = __ldcs(v4 + j);
+    adam_update4(pa, ga, ma, va, grp, 4 * j, b1, b2, eps, bc1, bc2);
+    __stcs(p4 + j, pa);
+    __stcs(m4 + j, ma);
+    __stcs(v4 + j, va);
+  }
+  // tail elements past the last full float4
+  if (blockIdx.x == 0 && threadIdx.x < (unsigned)(total - 4 * n4)) {
+    const int64_t idx = 4 * n4 + threadIdx.x;
+    const float lr = adam_lr(grp, idx);
+    m[idx] = b1 * m[idx] + (1.f - b1) * g[idx];
+    v[idx] = b2 * v[idx] + (1.f - b2) * g[idx] * g[idx];
+    p[idx] -= lr * (m[idx] * bc1) / (sqrtf(v[idx] * bc2) + eps);
+  }
+}
 
 // ------------------------------------------- Adam fused with the exchange
 // Data-parallel update of one rank's parameter shard over NVLink multicast
@@ -568,8 +598,12 @@ int fgs_adam_step(int64_t total, float* params, const float* grads, float* exp_a
     bc1 = 1.0f / (1.0f - powf(beta1, (float)step));
     bc2 = 1.0f / (1.0f - powf(beta2, (float)step));
   }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t n4 = (total + 3) / 4;
-  adam_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+  const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, (int64_t)sms * 8);
+  adam_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, (cudaStream_t)stream>>>(
       total, params, grads, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
   return check_launch("adam_step");
 }
