@@ -222,7 +222,7 @@ def main():
 
     # ---------------- value: everything resident in HBM
     tr.record = {"rasterize_backward", "rasterize_forward", "adam", "loss", "reduce", "allgather", "exchange",
-                 "preprocess_backward_train", "sort", "preprocess"}
+                 "preprocess_backward_train", "preprocess_backward_adam", "sort", "preprocess"}
     tr.events.clear()
     clocks = ClockSampler(local)
     clocks.start()
@@ -247,7 +247,8 @@ def main():
     bwd_ms = tr.kernel_ms("rasterize_backward")
     fwd_ms = tr.kernel_ms("rasterize_forward")
     stage_ms = {k: tr.kernel_ms(k) for k in ("preprocess", "sort", "loss", "preprocess_backward_train",
-                                              "adam", "reduce", "allgather", "exchange")}
+                                              "preprocess_backward_adam", "adam", "reduce", "allgather",
+                                              "exchange")}
     tr.record = set()
     t_max = torch.tensor([ms], device=dev)
     if pg is not None:

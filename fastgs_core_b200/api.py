@@ -52,7 +52,7 @@ def _f32(t, dev=None) -> torch.Tensor:
         t = t.to(dev)
     if not t.is_cuda:
         raise ValueError("fastgs_core_b200 runs on CUDA tensors only (no CPU path)")
-    return t.detach().to(torch.float32).contiguous()
+    return _aligned(t.detach().to(torch.float32).contiguous())
 
 
 def _int_t(t, dtype, dev) -> torch.Tensor:
@@ -61,7 +61,13 @@ def _int_t(t, dtype, dev) -> torch.Tensor:
         t = t.to(dev)
     if t.dtype != dtype:
         t = t.to(dtype)
-    return t.contiguous()
+    return _aligned(t.contiguous())
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """The kernels read several inputs as 8- and 16-byte vectors; a view that
+    starts inside an allocation is copied to a fresh (aligned) one."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
 def tile_grid(width: int, height: int) -> tuple[int, int]:

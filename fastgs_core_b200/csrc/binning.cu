@@ -368,6 +368,8 @@ int fgs_duplicate_with_keys(int32_t n, float mult, int32_t tile_bounds_x, int32_
   FGS_CHECK_ARG(xys && depths && point_offsets && conic_opacity && tiles_touched && keys_unsorted &&
                     values_unsorted,
                 "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(xys, 8) && FGS_ALIGNED(conic_opacity, 16),
+                "xys must be 8-byte, conic_opacity 16-byte aligned");
   FGS_CHECK_ARG(tile_bounds_x > 0 && tile_bounds_y > 0, "tile bounds must be positive");
   duplicate_kernel<<<(n + kDupThreads - 1) / kDupThreads, kDupThreads, 0, (cudaStream_t)stream>>>(
       n, mult, tile_bounds_x, tile_bounds_y, (const float2*)xys, depths, point_offsets,

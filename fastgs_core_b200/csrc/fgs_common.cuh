@@ -103,6 +103,19 @@ __device__ __forceinline__ float splat_power(float a, float b, float c, float dx
 // Otherwise -87 (the domain limit of fgs_expf_neg; fgs_expf is 0 below it).
 __device__ __forceinline__ float power_cut(float o) { return o <= 1.0f ? -5.55f : -87.0f; }
 
+// One Adam element update (torch.optim.Adam, no weight decay, bias corrections
+// passed as reciprocals bc1 = 1 / (1 - beta1^t), bc2 = 1 / (1 - beta2^t)), with
+// explicitly rounded operations so that every kernel that applies it (the
+// plain, the multicast and the one fused into the preprocess backward pass)
+// produces the same bits whatever its file's contraction setting.
+__device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g, float lr, float b1,
+                                          float b2, float eps, float bc1, float bc2) {
+  m = __fmaf_rn(b1, m, __fmul_rn(1.0f - b1, g));
+  v = __fmaf_rn(b2, v, __fmul_rn(__fmul_rn(1.0f - b2, g), g));
+  p = __fsub_rn(p, __fdiv_rn(__fmul_rn(lr, __fmul_rn(m, bc1)),
+                             __fadd_rn(__fsqrt_rn(__fmul_rn(v, bc2)), eps)));
+}
+
 __device__ __forceinline__ float fmin_t(float a, float b) { return b < a ? b : a; }
 __device__ __forceinline__ float fmax_t(float a, float b) { return a < b ? b : a; }
 __device__ __forceinline__ int imin(int a, int b) { return b < a ? b : a; }
@@ -177,6 +190,9 @@ inline void smem_attr_once(Kernel* k, int bytes, unsigned long long* done_mask) 
   }
 }
 }  // namespace fgs
+
+// pointers the kernels access as float2 / float4 / uint2 vectors
+#define FGS_ALIGNED(p, bytes) ((((uintptr_t)(p)) & ((bytes)-1)) == 0)
 
 #define FGS_CHECK_ARG(cond, ...)     \
   do {                               \

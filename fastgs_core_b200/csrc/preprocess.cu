@@ -373,13 +373,59 @@ struct PbwdArgs {
   float *g_means, *g_dc, *g_rest, *g_logit, *g_logscale, *g_rot;
   float *st_acc, *st_acc_abs, *st_denom, *st_max_radii;
   int accumulate;
+  // Adam fused in (kAdam): the flat raw parameters and moments in the
+  // gradient buffer's layout, one learning rate per attribute segment
+  float *ap, *am, *av;
+  float lr[6];
+  float b1, b2, eps, bc1, bc2;
 };
+
+// Shared-memory staging of the register-held gradients in the fused Adam
+// pass, per CTA: [segment][kPreThreads * width] at these offsets (units of
+// kPreThreads floats); 14 floats per Gaussian in all.
+enum { kAdamMeans = 0, kAdamDc = 3, kAdamLogit = 6, kAdamScale = 7, kAdamRot = 10, kAdamStaged = 14 };
+
+// Adam over one attribute segment of the flat layout (means 3, dc 3, sh rest
+// 45, opacity logit 1, log-scale 3, rotation 4 floats per Gaussian, each
+// segment attribute-major) for this CTA's Gaussians [base, base + cnt): a
+// contiguous run of cnt * width floats from seg + base * width, gradients in
+// shared memory in the same order. Four elements per thread per iteration so
+// that twelve loads are in flight.
+__device__ __forceinline__ void adam_block(const PbwdArgs& a, int64_t seg, int width, int base,
+                                           int cnt, const float* sgrad, float lr) {
+  float* __restrict__ P = a.ap + seg + (int64_t)base * width;
+  float* __restrict__ M = a.am + seg + (int64_t)base * width;
+  float* __restrict__ V = a.av + seg + (int64_t)base * width;
+  const int count = cnt * width;
+  for (int k0 = threadIdx.x; k0 < count; k0 += 4 * kPreThreads) {
+    float pv[4], mv[4], vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kPreThreads;
+      if (k < count) {
+        pv[u] = P[k];
+        mv[u] = M[k];
+        vv[u] = V[k];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kPreThreads;
+      if (k < count) {
+        adam_elem(pv[u], mv[u], vv[u], sgrad[k], lr, a.b1, a.b2, a.eps, a.bc1, a.bc2);
+        P[k] = pv[u];
+        M[k] = mv[u];
+        V[k] = vv[u];
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ v3 v3s(float s, v3 a) { return V3(s * a.x, s * a.y, s * a.z); }
 __device__ __forceinline__ v3 v3sr(v3 a, float s) { return V3(a.x * s, a.y * s, a.z * s); }
 __device__ __forceinline__ v3 v3add(v3 a, v3 b) { return V3(a.x + b.x, a.y + b.y, a.z + b.z); }
 
-template <bool kTrain>
+template <bool kTrain, bool kAdam>
 __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a) {
   extern __shared__ float s_buf[];  // [kPreThreads * S3]: staged sh, overwritten by dsh
   const fgs_preprocess_params& P = a.p;
@@ -695,31 +741,47 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
       float dls[3];
 #pragma unroll
       for (int c = 0; c < 3; ++c) dls[c] = dsc[c] * a.scales[3 * (int64_t)i + c];
-      const float4 qr = reinterpret_cast<const float4*>(a.quats_raw)[i];
+      // scalar accesses to the flat buffers: their rotation segment starts at
+      // 55 n floats, 16-byte aligned only when n is a multiple of 4
+      const float4 qr = make_float4(a.quats_raw[4 * (int64_t)i], a.quats_raw[4 * (int64_t)i + 1],
+                                    a.quats_raw[4 * (int64_t)i + 2], a.quats_raw[4 * (int64_t)i + 3]);
       const float qn = sqrtf(qr.x * qr.x + qr.y * qr.y + qr.z * qr.z + qr.w * qr.w);
       const float inv = 1.0f / (qn + 1e-8f);
       const float qdot = qr.x * dq[0] + qr.y * dq[1] + qr.z * dq[2] + qr.w * dq[3];
       const float corr = qn > 0.0f ? qdot * inv * inv / qn : 0.0f;
       const float dr[4] = {dq[0] * inv - qr.x * corr, dq[1] * inv - qr.y * corr,
                            dq[2] * inv - qr.z * corr, dq[3] * inv - qr.w * corr};
-      const bool acc = a.accumulate != 0;
+      if constexpr (kAdam) {
+        // staged for the CTA-wide, coalesced Adam pass at the end
+        float* sg = s_buf + kPreThreads * S3;
+        const int t = threadIdx.x;
 #pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        float* gm = a.g_means + 3 * (int64_t)i + c;
-        float* gd = a.g_dc + 3 * (int64_t)i + c;
-        float* gs = a.g_logscale + 3 * (int64_t)i + c;
-        *gm = acc ? *gm + dm[c] : dm[c];
-        *gd = acc ? *gd + ddc[c] : ddc[c];
-        *gs = acc ? *gs + dls[c] : dls[c];
+        for (int c = 0; c < 3; ++c) {
+          sg[kAdamMeans * kPreThreads + 3 * t + c] = dm[c];
+          sg[kAdamDc * kPreThreads + 3 * t + c] = ddc[c];
+          sg[kAdamScale * kPreThreads + 3 * t + c] = dls[c];
+        }
+        sg[kAdamLogit * kPreThreads + t] = dlogit;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sg[kAdamRot * kPreThreads + 4 * t + c] = dr[c];
+      } else {
+        const bool acc = a.accumulate != 0;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          float* gm = a.g_means + 3 * (int64_t)i + c;
+          float* gd = a.g_dc + 3 * (int64_t)i + c;
+          float* gs = a.g_logscale + 3 * (int64_t)i + c;
+          *gm = acc ? *gm + dm[c] : dm[c];
+          *gd = acc ? *gd + ddc[c] : ddc[c];
+          *gs = acc ? *gs + dls[c] : dls[c];
+        }
+        a.g_logit[i] = acc ? a.g_logit[i] + dlogit : dlogit;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float* gr = a.g_rot + 4 * (int64_t)i + c;
+          *gr = acc ? *gr + dr[c] : dr[c];
+        }
       }
-      a.g_logit[i] = acc ? a.g_logit[i] + dlogit : dlogit;
-      float4* gr = reinterpret_cast<float4*>(a.g_rot) + i;
-      float4 r4 = make_float4(dr[0], dr[1], dr[2], dr[3]);
-      if (acc) {
-        const float4 o4 = *gr;
-        r4 = make_float4(o4.x + r4.x, o4.y + r4.y, o4.z + r4.z, o4.w + r4.w);
-      }
-      *gr = r4;
       my_radius = a.radii[i];
       my_dvs = dvs;
       // densification statistics (scripts/train_scanner_fastgs.py:391-405)
@@ -739,7 +801,16 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
     }
     __syncthreads();
     float* gdst = dsh_dst + (int64_t)base * S3;
-    if (kTrain && a.accumulate) {
+    if (kAdam) {
+      const int64_t n = P.n;
+      const float* sg = s_buf + kPreThreads * S3;
+      adam_block(a, 0, 3, base, cnt, sg + kAdamMeans * kPreThreads, a.lr[0]);
+      adam_block(a, 3 * n, 3, base, cnt, sg + kAdamDc * kPreThreads, a.lr[1]);
+      adam_block(a, 6 * n, S3, base, cnt, s_dsh, a.lr[2]);
+      adam_block(a, 51 * n, 1, base, cnt, sg + kAdamLogit * kPreThreads, a.lr[3]);
+      adam_block(a, 52 * n, 3, base, cnt, sg + kAdamScale * kPreThreads, a.lr[4]);
+      adam_block(a, 55 * n, 4, base, cnt, sg + kAdamRot * kPreThreads, a.lr[5]);
+    } else if (kTrain && a.accumulate) {
       for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) gdst[k] += s_dsh[k];
     } else {
       for (int k = threadIdx.x; k < cnt * S3; k += blockDim.x) gdst[k] = s_dsh[k];
@@ -789,6 +860,10 @@ int fgs_preprocess_forward(const fgs_preprocess_params* p, const float* means3d,
   FGS_CHECK_ARG(radii && xys && depths && cov3d && rgb && conic_opacity && tiles_touched &&
                     clamped && viewspace_out,
                 "missing output pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(xys, 8) && FGS_ALIGNED(cov3d, 8) && FGS_ALIGNED(conic_opacity, 16) &&
+                    FGS_ALIGNED(viewspace_out, 16) && (p->use_cov3d_precomp || FGS_ALIGNED(quats, 16)),
+                "xys and cov3d must be 8-byte, conic_opacity, viewspace_out and rotations "
+                "16-byte aligned");
   PreArgs a;
   a.p = *p;
   a.focal_x = (float)p->image_width / (2.0f * p->tan_fovx);
@@ -854,6 +929,10 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
   FGS_CHECK_ARG(dL_dmeans3d && dL_ddc && dL_dcolors_precomp && dL_dopacities && dL_dscales &&
                     dL_dquats && dL_dviewspace_in && (p->max_sh_coeffs == 0 || dL_dsh),
                 "missing output pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(dL_dconic_opacity, 16) && FGS_ALIGNED(dL_dviewspace_out, 16) &&
+                    FGS_ALIGNED(dL_dquats, 16) && FGS_ALIGNED(dL_dviewspace_in, 16) &&
+                    (p->use_cov3d_precomp || FGS_ALIGNED(quats, 16)),
+                "rotations, conic and viewspace gradients must be 16-byte aligned");
   PbwdArgs a;
   memset(&a, 0, sizeof(a));
   a.p = *p;
@@ -868,9 +947,9 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
   const bool sh_path = !p->use_colors_precomp && p->max_sh_coeffs > 0;
   const size_t smem = sh_path ? (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
   static unsigned long long attr_done = 0;
-  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<false>, (int)smem, &attr_done);
+  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<false, false>, (int)smem, &attr_done);
   const int blocks = (p->n + kPreThreads - 1) / kPreThreads;
-  preprocess_bwd_kernel<false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  preprocess_bwd_kernel<false, false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_backward");
 }
 
@@ -893,6 +972,9 @@ int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* m
                     cam_pos && sh && cov3d_fwd && dL_drgb && dL_dxys && dL_dconic_opacity &&
                     dL_dviewspace && radii && clamped && grad_flat && stats,
                 "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(quats, 16) && FGS_ALIGNED(dL_dconic_opacity, 16) &&
+                    FGS_ALIGNED(dL_dviewspace, 16),
+                "rotations, conic and viewspace gradients must be 16-byte aligned");
   const int64_t n = p->n;
   PbwdArgs a;
   memset(&a, 0, sizeof(a));
@@ -917,10 +999,70 @@ int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* m
   a.accumulate = accumulate;
   const size_t smem = (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float);
   static unsigned long long attr_done = 0;
-  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<true>, (int)smem, &attr_done);
+  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<true, false>, (int)smem, &attr_done);
   const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
-  preprocess_bwd_kernel<true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  preprocess_bwd_kernel<true, false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_backward_train");
+}
+
+int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* scales,
+                                 const float* quats, const float* opacities,
+                                 const float* viewmatrix, const float* projmatrix,
+                                 const float* cam_pos, const float* cov3d_fwd, const float* dL_drgb,
+                                 const float* dL_dxys, const float* dL_dconic_opacity,
+                                 const float* dL_dviewspace, const int32_t* radii,
+                                 const uint8_t* clamped, float* params, float* exp_avg,
+                                 float* exp_avg_sq, const float* group_lr, float beta1, float beta2,
+                                 float eps, int32_t step, int32_t bias_correction, float* stats,
+                                 void* stream) {
+  int st = validate_pre(p);
+  if (st) return st;
+  if (p->n == 0) return FGS_OK;
+  FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
+                "training mode needs the scales+quats and dc+sh paths");
+  FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
+  FGS_CHECK_ARG(scales && quats && opacities && viewmatrix && projmatrix && cam_pos && cov3d_fwd &&
+                    dL_drgb && dL_dxys && dL_dconic_opacity && dL_dviewspace && radii && clamped &&
+                    params && exp_avg && exp_avg_sq && group_lr && stats,
+                "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(quats, 16) && FGS_ALIGNED(dL_dconic_opacity, 16) &&
+                    FGS_ALIGNED(dL_dviewspace, 16),
+                "rotations, conic and viewspace gradients must be 16-byte aligned");
+  FGS_CHECK_ARG(!bias_correction || step >= 1, "step must be >= 1 with bias correction");
+  const int64_t n = p->n;
+  PbwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.p = *p;
+  a.focal_x = 0.5f * (float)p->image_width / (p->tan_fovx < 1e-6f ? 1e-6f : p->tan_fovx);
+  a.focal_y = 0.5f * (float)p->image_height / (p->tan_fovy < 1e-6f ? 1e-6f : p->tan_fovy);
+  // the raw means, sh rest and rotations are read from the parameter buffer
+  // that this launch updates: each Gaussian's values are read before its own
+  // update, and the sh rows are staged in shared memory first
+  a.means3d = params; a.sh = params + 6 * n; a.quats_raw = params + 55 * n;
+  a.scales = scales; a.quats = quats; a.vm = viewmatrix; a.pm = projmatrix;
+  a.cam_pos = cam_pos; a.cov3d_fwd = cov3d_fwd;
+  a.drgb = dL_drgb; a.dxys = dL_dxys; a.dconic = dL_dconic_opacity; a.dvs_out = dL_dviewspace;
+  a.radii = radii; a.clamped = clamped;
+  a.opac_act = opacities;
+  a.st_acc = stats;
+  a.st_acc_abs = stats + n;
+  a.st_denom = stats + 2 * n;
+  a.st_max_radii = stats + 3 * n;
+  a.ap = params;
+  a.am = exp_avg;
+  a.av = exp_avg_sq;
+  for (int k = 0; k < 6; ++k) a.lr[k] = group_lr[k];
+  a.b1 = beta1;
+  a.b2 = beta2;
+  a.eps = eps;
+  a.bc1 = bias_correction ? 1.0f / (1.0f - powf(beta1, (float)step)) : 1.0f;
+  a.bc2 = bias_correction ? 1.0f / (1.0f - powf(beta2, (float)step)) : 1.0f;
+  const size_t smem = (size_t)kPreThreads * (p->max_sh_coeffs * 3 + kAdamStaged) * sizeof(float);
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<true, true>, (int)smem, &attr_done);
+  const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
+  preprocess_bwd_kernel<true, true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  return check_launch("preprocess_backward_adam");
 }
 
 }  // extern "C"

@@ -267,6 +267,8 @@ int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
                                        bucket_to_tile && sampled_t && sampled_ar),
                 "missing pointer");
   FGS_CHECK_ARG(!p->get_flag || (metric_map && metric_count), "get_flag needs metric_map / metric_count");
+  FGS_CHECK_ARG(FGS_ALIGNED(ranges, 8) && FGS_ALIGNED(means2d, 8) && FGS_ALIGNED(conic_opacity, 16),
+                "ranges and means2d must be 8-byte, conic_opacity 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   FwdArgs a;
   a.W = p->image_width;

@@ -419,6 +419,8 @@ int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
                     final_t && n_contrib && max_contrib && pixel_colors && dL_dmeans2d &&
                     dL_dcolors && dL_dconic_opacity && dL_dviewspace,
                 "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(ranges, 8) && FGS_ALIGNED(means2d, 8) && FGS_ALIGNED(conic_opacity, 16),
+                "ranges and means2d must be 8-byte, conic_opacity 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   BwdArgs a;
   a.W = p->image_width;

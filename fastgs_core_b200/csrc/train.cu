@@ -25,7 +25,10 @@ __global__ void activate_kernel(int64_t n, const float* __restrict__ flat, float
   opac[i] = 1.0f / (1.0f + expf(-lg));
 #pragma unroll
   for (int c = 0; c < 3; ++c) scales[3 * i + c] = expf(flat[52 * n + 3 * i + c]);
-  const float4 q = reinterpret_cast<const float4*>(flat + 55 * n)[i];
+  // scalar loads: the rotation segment starts at 55 n floats, 16-byte aligned
+  // only when n is a multiple of 4
+  const float* qp = flat + 55 * n + 4 * i;
+  const float4 q = make_float4(qp[0], qp[1], qp[2], qp[3]);
   const float inv = 1.0f / (sqrtf(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w) + 1e-8f);
   reinterpret_cast<float4*>(quats)[i] = make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
 }
@@ -306,9 +309,7 @@ __device__ __forceinline__ void adam_update4(float4& pp, const float4 gg, float4
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const float lr = same ? lr0 : adam_lr(grp, i + k);
-    ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
-    va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
-    pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
+    adam_elem(pa[k], ma[k], va[k], ga[k], lr, b1, b2, eps, bc1, bc2);
   }
 }
 
@@ -354,9 +355,11 @@ __global__ void __launch_bounds__(256) adam_kernel(int64_t total, float* __restr
   if (blockIdx.x == 0 && threadIdx.x < (unsigned)(total - 4 * n4)) {
     const int64_t idx = 4 * n4 + threadIdx.x;
     const float lr = adam_lr(grp, idx);
-    m[idx] = b1 * m[idx] + (1.f - b1) * g[idx];
-    v[idx] = b2 * v[idx] + (1.f - b2) * g[idx] * g[idx];
-    p[idx] -= lr * (m[idx] * bc1) / (sqrtf(v[idx] * bc2) + eps);
+    float pv = p[idx], mv = m[idx], vv = v[idx];
+    adam_elem(pv, mv, vv, g[idx], lr, b1, b2, eps, bc1, bc2);
+    p[idx] = pv;
+    m[idx] = mv;
+    v[idx] = vv;
   }
 }
 
@@ -398,9 +401,7 @@ __device__ __forceinline__ void adam4(float4& pp, float4& mm, float4& vv, const 
         lr = grp.lr[q];
         break;
       }
-    ma[k] = b1 * ma[k] + (1.f - b1) * ga[k];
-    va[k] = b2 * va[k] + (1.f - b2) * ga[k] * ga[k];
-    pa[k] -= lr * (ma[k] * bc1) / (sqrtf(va[k] * bc2) + eps);
+    adam_elem(pa[k], ma[k], va[k], ga[k], lr, b1, b2, eps, bc1, bc2);
   }
 }
 
@@ -542,6 +543,7 @@ int fgs_activate_params(int64_t n, const float* params_flat, float* opacities, f
   FGS_CHECK_ARG(n >= 0, "n must be >= 0");
   if (n == 0) return FGS_OK;
   FGS_CHECK_ARG(params_flat && opacities && scales && quats, "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(quats, 16), "rotations output must be 16-byte aligned");
   activate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
       n, params_flat, opacities, scales, quats);
   return check_launch("activate_params");

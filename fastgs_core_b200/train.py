@@ -218,12 +218,16 @@ class Trainer:
         self.record = set()
         # forward pass records contributing pairs for the backward pass
         self.contrib_mask = os.environ.get("FGS_CONTRIB_MASK", "1") != "0"
+        # one view on one rank: Adam fused into the backward pass (no
+        # gradient buffer round trip); the gradient buffer is then not written
+        self.fuse_adam = os.environ.get("FGS_FUSE_ADAM", "1") != "0"
         self.events: dict[str, list] = {}
         self.launches = 0
 
     # kernels each C entry point launches (memsets are not kernels)
     _KERNELS = {"preprocess": 1, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
-                "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1, "activate": 1,
+                "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1,
+                "preprocess_backward_adam": 1, "activate": 1,
                 "adam": 1}
 
     def _call(self, name, fn, *args):
@@ -275,9 +279,13 @@ class Trainer:
     def _stream(self):
         return C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
 
-    def render_view(self, cam, target=None, accumulate=False, loss_out=None, loss_scale=1.0):
+    def render_view(self, cam, target=None, accumulate=False, loss_out=None, loss_scale=1.0,
+                    fused_adam=False):
         """Forward (and, with a target, loss + backward accumulated into the
-        flat gradient buffer) of one view. Returns the image [3, H*W]."""
+        flat gradient buffer) of one view. Returns the image [3, H*W]. With
+        fused_adam the backward pass applies the Adam step (of step number
+        self.step_count) to the parameters directly instead of writing the
+        gradient buffer: for a step whose gradient is this one view's."""
         L = lib()
         n, d, ws = self.n, self.dev, self.ws
         W, H = int(cam.width), int(cam.height)
@@ -377,12 +385,28 @@ class Trainer:
         self._call("loss", L.fgs_l1_dssim_loss, W, H, _p(img), _p(target), self.w_l1 * loss_scale,
                                   self.w_ssim * loss_scale, _p(lout), _p(dimg), _p(lscr), st)
         # backward
-        g2 = ws.get("g_raster", 13 * n, torch.float32)
+        # one zeroed buffer, each part starting on a 16-byte boundary (the
+        # kernels read the conic and viewspace gradients as float4)
+        o1 = -(-2 * n // 4) * 4
+        o2 = o1 + -(-3 * n // 4) * 4
+        g2 = ws.get("g_raster", o2 + 8 * n, torch.float32)
         g2.zero_()
-        dmeans2d, dcolors, dconic, dvs = g2[:2 * n], g2[2 * n:5 * n], g2[5 * n:9 * n], g2[9 * n:13 * n]
+        dmeans2d, dcolors = g2[:2 * n], g2[o1:o1 + 3 * n]
+        dconic, dvs = g2[o2:o2 + 4 * n], g2[o2 + 4 * n:o2 + 8 * n]
+        self.raster_grads = (dmeans2d, dcolors, dconic, dvs)
         self._call("rasterize_backward", L.fgs_rasterize_backward, C.byref(rp), _p(ranges), _p(svals), _p(boffs), _p(xys), _p(rgb), _p(conic),
             _p(self.background), _p(dimg), _p(b2t), _p(samp_t), _p(samp_ar), _p(final_t),
             _p(ncontrib), _p(maxc), _p(pixc), _p(dmeans2d), _p(dcolors), _p(dconic), _p(dvs), st)
+        if fused_adam:
+            lr = self.lrs
+            lrs = (C.c_float * 6)(lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations)
+            self._call("preprocess_backward_adam", L.fgs_preprocess_backward_adam, C.byref(prm),
+                       _p(self.scales), _p(self.quats), _p(self.opacities), _p(vm), _p(pm), _p(cp),
+                       _p(cov3d), _p(dcolors), _p(dmeans2d), _p(dconic), _p(dvs), _p(radii),
+                       _p(clamped), _p(self.params), _p(self.exp_avg), _p(self.exp_avg_sq), lrs,
+                       float(self.betas[0]), float(self.betas[1]), self.eps, self.step_count,
+                       int(self.bias_correction), _p(self.step_stats), st)
+            return img
         self._call("preprocess_backward_train", L.fgs_preprocess_backward_train, C.byref(prm), _p(means), _p(self.scales), _p(self.quats), _p(self.view("rotations")),
             _p(self.opacities), _p(vm), _p(pm), _p(cp), _p(rest), _p(cov3d), _p(dcolors),
             _p(dmeans2d), _p(dconic), _p(dvs), _p(radii), _p(clamped), int(bool(accumulate)),
@@ -412,6 +436,13 @@ class Trainer:
         self.activate()
         self.step_stats.zero_()
         scale = 1.0 / max(len(cams), 1)  # mean loss over the whole batch
+        if self.fuse_adam and world == 1 and len(mine) == 1:
+            # the gradient is this one view's: Adam runs inside its backward pass
+            self.step_count += 1
+            self.render_view(cams[mine[0]], targets[mine[0]], loss_out=loss_out, loss_scale=scale,
+                             fused_adam=True)
+            fold_stats(self.stats, self.step_stats, self.n)
+            return 1
         if not mine:
             self.grads.zero_()
         for j, v in enumerate(mine):

@@ -290,6 +290,27 @@ FGS_API int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const 
                                           const uint8_t* clamped, int32_t accumulate,
                                           float* grad_flat, float* stats, void* stream);
 
+/* fgs_preprocess_backward_train of one view followed by the Adam step of
+ * fgs_adam_step, in one pass: each Gaussian's raw-parameter gradients are
+ * applied to params / exp_avg / exp_avg_sq (flat layout, 59 n floats: means
+ * 3, dc 3, sh rest 45, opacity logit 1, log-scale 3, rotation 4, each segment
+ * attribute-major) as soon as they are formed, so no gradient buffer is
+ * written or read. group_lr[6] holds the learning rate of each segment in that
+ * order. The raw means, sh rest and rotations are read from params. For a
+ * step whose gradient is exactly this one view's (one view, one rank); the
+ * result equals fgs_preprocess_backward_train + fgs_adam_step bit for bit. */
+FGS_API int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* scales,
+                                         const float* quats, const float* opacities,
+                                         const float* viewmatrix, const float* projmatrix,
+                                         const float* cam_pos, const float* cov3d_fwd,
+                                         const float* dL_drgb, const float* dL_dxys,
+                                         const float* dL_dconic_opacity,
+                                         const float* dL_dviewspace, const int32_t* radii,
+                                         const uint8_t* clamped, float* params, float* exp_avg,
+                                         float* exp_avg_sq, const float* group_lr, float beta1,
+                                         float beta2, float eps, int32_t step,
+                                         int32_t bias_correction, float* stats, void* stream);
+
 /* loss = w_l1 * mean|image - target| + w_ssim * (1 - mean SSIM(image, target))
  * over CHW [3,H,W] float images (SSIM: 11x11 Gaussian window, sigma 1.5, zero
  * padding, C1 = 0.01^2, C2 = 0.03^2), and dL/dimage. loss_out receives

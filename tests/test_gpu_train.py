@@ -140,6 +140,7 @@ def test_trainer_step_applies_adam(cuda_dev):
     scene, cam = S.small_scene(32, 2000, 3, 64, 64)
     target = torch.rand(3 * 64 * 64, generator=torch.Generator().manual_seed(4)).to(cuda_dev)
     tr = Trainer(scene, cuda_dev)
+    tr.fuse_adam = False  # the separate Adam launch, which leaves the gradient readable
     p0 = tr.params.clone()
     lo = torch.zeros(4, device=cuda_dev)
     tr.step([cam], [target], loss_out=lo)
@@ -188,3 +189,73 @@ def test_metric_map_and_scores(cuda_dev):
     want = (want - want.min()) / max(want.max() - want.min(), 1e-6)
     np.testing.assert_allclose(pr.cpu().numpy(), want, rtol=1e-5, atol=1e-6)
     assert np.allclose(sa.cpu().numpy(), 3 * photometric * counts.float().cpu().numpy(), rtol=1e-5)
+
+
+def test_adam_fused_into_backward_matches_separate(cuda_dev):
+    """fgs_preprocess_backward_adam equals fgs_preprocess_backward_train +
+    fgs_adam_step bit for bit on the same inputs (n not a multiple of 4: the
+    attribute segments of the flat buffer are not 16-byte aligned)."""
+    import ctypes as C
+
+    from fastgs_core_b200._lib import PreprocessParams, lib
+
+    scene, cam = S.small_scene(33, 2003, 3, 80, 48)
+    n = scene.n
+    target = torch.rand(3 * 80 * 48, generator=torch.Generator().manual_seed(5)).to(cuda_dev)
+    tr = Trainer(scene, cuda_dev, bias_correction=True)
+    tr.fuse_adam = False
+    tr.step([cam], [target])  # non-zero moments
+    tr.activate()
+    tr.render_view(cam, target)  # leaves this view's backward inputs in the workspace
+    torch.cuda.synchronize()
+    ws = tr.ws.b
+    cm = ws["cam"][:35]
+    gm, gc, gk, gv = tr.raster_grads
+    prm = PreprocessParams(n, 3, 15, 1.0, 1.0, float(cam.tan_fovx), float(cam.tan_fovy), 80, 48, 0, 0)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    lrs = (C.c_float * 6)(3e-3, 1e-3, 5e-5, 1e-2, 5e-3, 1e-3)
+    total = 59 * n
+    P1, P2 = tr.params.clone(), tr.params.clone()
+    M1, M2 = tr.exp_avg[:total].clone(), tr.exp_avg[:total].clone()
+    V1, V2 = tr.exp_avg_sq[:total].clone(), tr.exp_avg_sq[:total].clone()
+    G = torch.empty(total, device=cuda_dev)
+    st1, st2 = torch.zeros(4 * n, device=cuda_dev), torch.zeros(4 * n, device=cuda_dev)
+    common = [p(tr.scales), p(tr.quats)]
+    L = lib()
+    assert L.fgs_preprocess_backward_train(
+        C.byref(prm), p(P1), *common, p(P1[55 * n:]), p(tr.opacities), p(cm[0:16]), p(cm[16:32]),
+        p(cm[32:35]), p(P1[6 * n:]), p(ws["cov3d"]), p(gc), p(gm), p(gk), p(gv), p(ws["radii"]), p(ws["clamped"]), 0, p(G), p(st1),
+        None) == 0
+    ends = (C.c_int64 * 6)(*[k * n for k in (3, 6, 51, 52, 55, 59)])
+    assert L.fgs_adam_step(total, p(P1), p(G), p(M1), p(V1), 6, ends, lrs, 0.9, 0.99, 1e-8, 2, 1,
+                           None) == 0
+    assert L.fgs_preprocess_backward_adam(
+        C.byref(prm), *common, p(tr.opacities), p(cm[0:16]), p(cm[16:32]), p(cm[32:35]),
+        p(ws["cov3d"]), p(gc), p(gm), p(gk), p(gv),
+        p(ws["radii"]), p(ws["clamped"]), p(P2), p(M2), p(V2), lrs, 0.9, 0.99, 1e-8, 2, 1, p(st2),
+        None) == 0
+    torch.cuda.synchronize()
+    assert not torch.equal(P1, tr.params)
+    assert torch.equal(P1, P2)
+    assert torch.equal(M1, M2)
+    assert torch.equal(V1, V2)
+    assert torch.equal(st1, st2)
+
+
+def test_trainer_fused_adam_step(cuda_dev):
+    """The trainer's one-view step with Adam fused into the backward pass
+    follows the separate path (within the float-atomic noise of the raster
+    backward; eps = 1 keeps Adam from amplifying it)."""
+    scene, cam = S.small_scene(34, 1999, 3, 64, 64)
+    target = torch.rand(3 * 64 * 64, generator=torch.Generator().manual_seed(6)).to(cuda_dev)
+    trs = [Trainer(scene, cuda_dev, eps=1.0), Trainer(scene, cuda_dev, eps=1.0)]
+    trs[1].fuse_adam = False
+    p0 = trs[0].params.clone()
+    for tr in trs:
+        for _ in range(3):
+            tr.step([cam], [target])
+    torch.cuda.synchronize()
+    a, b = trs
+    assert a.step_count == b.step_count == 3
+    assert rel_err((a.params - p0).cpu().numpy(), (b.params - p0).cpu().numpy()) < 1e-3
+    assert rel_err(a.stats.cpu().numpy(), b.stats.cpu().numpy()) < 1e-3
