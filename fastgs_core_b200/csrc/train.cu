@@ -81,29 +81,34 @@ __global__ void __launch_bounds__(256)
     sy[r * (kFI + 1) + q] = in ? yc[(size_t)gy * W + gx] : 0.0f;
   }
   __syncthreads();
-  // horizontal moments: each item is a row segment of kSeg outputs computed
-  // from one sliding window of kSeg + 10 inputs held in registers
-  constexpr int kSeg = 6;
-  constexpr int kHSeg = kFM / kSeg;  // 7 segments of 6 over 42 columns
+  // Work items below are sized so that each pass fills the CTA's 256 threads
+  // in whole rounds (the passes are separated by barriers).
+  // Horizontal moments: 52 rows x 14 segments of 3 outputs (728 items); each
+  // item keeps its 13-input window and the window's products in registers.
+  constexpr int kSeg = 3;
+  constexpr int kHSeg = kFM / kSeg;  // 14
   for (int k = t; k < kFI * kHSeg; k += 256) {
     const int r = k / kHSeg, q0 = (k % kHSeg) * kSeg;
-    float xv[kSeg + 10], yv[kSeg + 10];
+    float xv[kSeg + 10], yv[kSeg + 10], xx[kSeg + 10], yy[kSeg + 10], xy[kSeg + 10];
 #pragma unroll
     for (int i = 0; i < kSeg + 10; ++i) {
       xv[i] = sx[r * (kFI + 1) + q0 + i];
       yv[i] = sy[r * (kFI + 1) + q0 + i];
+      xx[i] = xv[i] * xv[i];
+      yy[i] = yv[i] * yv[i];
+      xy[i] = xv[i] * yv[i];
     }
 #pragma unroll
     for (int o = 0; o < kSeg; ++o) {
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
 #pragma unroll
       for (int j = 0; j < 11; ++j) {
-        const float w = c_win[j], xx = xv[o + j], yy = yv[o + j];
-        a0 += w * xx;
-        a1 += w * yy;
-        a2 += w * xx * xx;
-        a3 += w * yy * yy;
-        a4 += w * xx * yy;
+        const float w = c_win[j];
+        a0 += w * xv[o + j];
+        a1 += w * yv[o + j];
+        a2 += w * xx[o + j];
+        a3 += w * yy[o + j];
+        a4 += w * xy[o + j];
       }
       sh[(0 * kFI + r) * kFM + q0 + o] = a0;
       sh[(1 * kFI + r) * kFM + q0 + o] = a1;
@@ -113,26 +118,25 @@ __global__ void __launch_bounds__(256)
     }
   }
   __syncthreads();
-  // vertical moments, SSIM and its derivatives on the 42x42 map region:
-  // each item is a column segment of kSeg rows. The maps overwrite the input
-  // window, so every item is computed before any is stored.
+  // Vertical moments, SSIM and its derivatives on the 42x42 map region: 42
+  // columns x 6 segments of 7 rows (252 items, one round). The maps overwrite
+  // the input window, so every item is computed before any is stored.
   float ssum = 0.f, lsum = 0.f;
-  constexpr int kV1Items = kFM * kHSeg;  // 294
-  constexpr int kV1PerThread = (kV1Items + 255) / 256;
-  float dm[kV1PerThread][3][kSeg];
-#pragma unroll
-  for (int it = 0; it < kV1PerThread; ++it) {
-    const int k = t + it * 256;
-    if (k >= kV1Items) break;
-    const int q = k % kFM, r0 = (k / kFM) * kSeg;
-    float m[5][kSeg];
+  constexpr int kVSeg = 7;
+  constexpr int kV1Items = kFM * (kFM / kVSeg);  // 252
+  static_assert(kV1Items <= 256, "one vertical item per thread");
+  float dm[3][kVSeg];
+  const bool v1 = t < kV1Items;
+  const int vq = t % kFM, vr0 = (t / kFM) * kVSeg;
+  if (v1) {
+    float m[5][kVSeg];
 #pragma unroll
     for (int qq = 0; qq < 5; ++qq) {
-      float col[kSeg + 10];
+      float col[kVSeg + 10];
 #pragma unroll
-      for (int i = 0; i < kSeg + 10; ++i) col[i] = sh[(qq * kFI + r0 + i) * kFM + q];
+      for (int i = 0; i < kVSeg + 10; ++i) col[i] = sh[(qq * kFI + vr0 + i) * kFM + vq];
 #pragma unroll
-      for (int o = 0; o < kSeg; ++o) {
+      for (int o = 0; o < kVSeg; ++o) {
         float acc = 0.f;
 #pragma unroll
         for (int j = 0; j < 11; ++j) acc += c_win[j] * col[o + j];
@@ -140,9 +144,9 @@ __global__ void __launch_bounds__(256)
       }
     }
 #pragma unroll
-    for (int o = 0; o < kSeg; ++o) {
-      const int r = r0 + o;
-      const int gy = y0 - kR + r, gx = x0 - kR + q;
+    for (int o = 0; o < kVSeg; ++o) {
+      const int r = vr0 + o;
+      const int gy = y0 - kR + r, gx = x0 - kR + vq;
       float d_mu = 0.f, d_exx = 0.f, d_exy = 0.f;
       if (gx >= 0 && gx < W && gy >= 0 && gy < H) {
         const float mu_x = m[0][o], mu_y = m[1][o], exx = m[2][o], eyy = m[3][o], exy = m[4][o];
@@ -156,57 +160,56 @@ __global__ void __launch_bounds__(256)
         d_mu = 2.f * mu_y * (B - A) * inv - 2.f * mu_x * ssim * (1.f / Cc - 1.f / D);
         d_exx = -ssim / D;
         d_exy = 2.f * A * inv;
-        if (r >= kR && r < kR + kFO && q >= kR && q < kR + kFO) ssum += ssim;  // own pixels
+        if (r >= kR && r < kR + kFO && vq >= kR && vq < kR + kFO) ssum += ssim;  // own pixels
       }
-      dm[it][0][o] = d_mu;
-      dm[it][1][o] = d_exx;
-      dm[it][2][o] = d_exy;
+      dm[0][o] = d_mu;
+      dm[1][o] = d_exx;
+      dm[2][o] = d_exy;
     }
   }
   __syncthreads();  // the input window is dead from here on
+  if (v1) {
 #pragma unroll
-  for (int it = 0; it < kV1PerThread; ++it) {
-    const int k = t + it * 256;
-    if (k >= kV1Items) break;
-    const int q = k % kFM, r0 = (k / kFM) * kSeg;
-#pragma unroll
-    for (int o = 0; o < kSeg; ++o) {
-      mp[(0 * kFM + r0 + o) * (kFM + 1) + q] = dm[it][0][o];
-      mp[(1 * kFM + r0 + o) * (kFM + 1) + q] = dm[it][1][o];
-      mp[(2 * kFM + r0 + o) * (kFM + 1) + q] = dm[it][2][o];
+    for (int o = 0; o < kVSeg; ++o) {
+      mp[(0 * kFM + vr0 + o) * (kFM + 1) + vq] = dm[0][o];
+      mp[(1 * kFM + vr0 + o) * (kFM + 1) + vq] = dm[1][o];
+      mp[(2 * kFM + vr0 + o) * (kFM + 1) + vq] = dm[2][o];
     }
   }
   __syncthreads();
-  // horizontal convolution of the derivative maps: row segments of 8
+  // Horizontal convolution of the derivative maps: 3 maps x 42 rows x 4
+  // segments of 8 outputs (504 items, two rounds)
   constexpr int kSeg2 = 8;
-  for (int k = t; k < kFM * (kFO / kSeg2); k += 256) {
-    const int r = k / (kFO / kSeg2), q0 = (k % (kFO / kSeg2)) * kSeg2;
+  for (int k = t; k < 3 * kFM * (kFO / kSeg2); k += 256) {
+    const int qq = k / (kFM * (kFO / kSeg2));
+    const int rem = k % (kFM * (kFO / kSeg2));
+    const int r = rem / (kFO / kSeg2), q0 = (rem % (kFO / kSeg2)) * kSeg2;
+    float row[kSeg2 + 10];
 #pragma unroll
-    for (int qq = 0; qq < 3; ++qq) {
-      float row[kSeg2 + 10];
+    for (int i = 0; i < kSeg2 + 10; ++i) row[i] = mp[(qq * kFM + r) * (kFM + 1) + q0 + i];
 #pragma unroll
-      for (int i = 0; i < kSeg2 + 10; ++i) row[i] = mp[(qq * kFM + r) * (kFM + 1) + q0 + i];
+    for (int o = 0; o < kSeg2; ++o) {
+      float acc = 0.f;
 #pragma unroll
-      for (int o = 0; o < kSeg2; ++o) {
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < 11; ++j) acc += c_win[j] * row[o + j];
-        h2[(qq * kFM + r) * kFO + q0 + o] = acc;
-      }
+      for (int j = 0; j < 11; ++j) acc += c_win[j] * row[o + j];
+      h2[(qq * kFM + r) * kFO + q0 + o] = acc;
     }
   }
   __syncthreads();
-  // vertical convolution and the image gradient: column segments of 8
-  for (int k = t; k < kFO * (kFO / kSeg2); k += 256) {
-    const int q = k % kFO, r0 = (k / kFO) * kSeg2;
-    float g[3][kSeg2];
+  // Vertical convolution and the image gradient: 32 columns x 8 segments of
+  // 4 rows (256 items, one round)
+  constexpr int kSeg3 = 4;
+  static_assert(kFO * (kFO / kSeg3) == 256, "one final item per thread");
+  {
+    const int q = t % kFO, r0 = (t / kFO) * kSeg3;
+    float g[3][kSeg3];
 #pragma unroll
     for (int qq = 0; qq < 3; ++qq) {
-      float col[kSeg2 + 10];
+      float col[kSeg3 + 10];
 #pragma unroll
-      for (int i = 0; i < kSeg2 + 10; ++i) col[i] = h2[(qq * kFM + r0 + i) * kFO + q];
+      for (int i = 0; i < kSeg3 + 10; ++i) col[i] = h2[(qq * kFM + r0 + i) * kFO + q];
 #pragma unroll
-      for (int o = 0; o < kSeg2; ++o) {
+      for (int o = 0; o < kSeg3; ++o) {
         float acc = 0.f;
 #pragma unroll
         for (int j = 0; j < 11; ++j) acc += c_win[j] * col[o + j];
@@ -214,7 +217,7 @@ __global__ void __launch_bounds__(256)
       }
     }
 #pragma unroll
-    for (int o = 0; o < kSeg2; ++o) {
+    for (int o = 0; o < kSeg3; ++o) {
       const int r = r0 + o;
       const int gy = y0 + r, gx = x0 + q;
       if (gx >= W || gy >= H) continue;
