@@ -157,6 +157,19 @@ def run_reference(args):
     return 0
 
 
+_STDOUT_FD = None
+
+
+def _emit(line: dict) -> None:
+    """Print the one JSON result line on the real standard output."""
+    sys.stdout.flush()
+    if _STDOUT_FD is not None:
+        os.dup2(_STDOUT_FD, 1)
+    print(json.dumps(line), flush=True)
+    if _STDOUT_FD is not None:
+        os.dup2(2, 1)  # whatever prints at shutdown goes to stderr too
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -168,6 +181,12 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    # Libraries print banners to file descriptor 1 (NCCL's version line among
+    # them): until the result line, descriptor 1 points at stderr.
+    global _STDOUT_FD
+    sys.stdout.flush()
+    _STDOUT_FD = os.dup(1)
+    os.dup2(2, 1)
 
     import torch
     import torch.distributed as dist
@@ -340,7 +359,7 @@ def main():
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(1)
-        print(json.dumps(line), flush=True)
+        _emit(line)
     if pg is not None:
         dist.barrier()
         dist.destroy_process_group()
