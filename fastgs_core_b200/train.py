@@ -218,6 +218,7 @@ class Trainer:
         self.record = set()
         # forward pass records contributing pairs for the backward pass
         self.contrib_mask = os.environ.get("FGS_CONTRIB_MASK", "1") != "0"
+        self._key_cap = 0  # capacity of the grow-only key buffers
         # one view on one rank: Adam fused into the backward pass (no
         # gradient buffer round trip); the gradient buffer is then not written
         self.fuse_adam = os.environ.get("FGS_FUSE_ADAM", "1") != "0"
@@ -280,7 +281,7 @@ class Trainer:
         return C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
 
     def render_view(self, cam, target=None, accumulate=False, loss_out=None, loss_scale=1.0,
-                    fused_adam=False):
+                    fused_adam=False, stats=None):
         """Forward (and, with a target, loss + backward accumulated into the
         flat gradient buffer) of one view. Returns the image [3, H*W]. With
         fused_adam the backward pass applies the Adam step (of step number
@@ -330,17 +331,32 @@ class Trainer:
         scan_scr = ws.get("scan_scr", int(L.fgs_scan_scratch_bytes(n)), torch.uint8)
         self._call("scan", L.fgs_inclusive_scan_u32, n, _p(tiles), _p(offsets), _p(total), _p(scan_scr), st)
         self.k_host.copy_(total, non_blocking=True)
-        torch.cuda.current_stream(d).synchronize()  # the one host sync: K sizes the key buffers
+        k_ready = torch.cuda.Event()
+        k_ready.record(torch.cuda.current_stream(d))
+        # Duplicate-with-keys runs before the host knows K, into grow-only
+        # buffers of the capacity the previous views needed (its writes stop at
+        # the capacity); the host only waits for the count, and repeats the
+        # launch with larger buffers in the rare view that outgrows them.
+        cap = self._key_cap
+        if cap > 0:
+            keys = ws.get("keys", cap, torch.uint64)
+            vals = ws.get("vals", cap, torch.uint32)
+            self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
+                       _p(conic), _p(tiles), cap, _p(keys), _p(vals), st)
+        k_ready.synchronize()  # the one host sync: K sizes the sort and the bucket arrays
         K = int(self.k_host.item())
         self.last_rendered = K
         img = ws.get("img", 3 * P, torch.float32)
         if K == 0:
             img.view(3, P).copy_(self.background.view(3, 1).expand(3, P))
             return img
-        keys = ws.get("keys", K, torch.uint64)
-        vals = ws.get("vals", K, torch.uint32)
-        self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets), _p(conic),
-                                        _p(tiles), K, _p(keys), _p(vals), st)
+        if K > cap:
+            cap = self._key_cap = K + K // 4 + 1024
+            keys = ws.get("keys", cap, torch.uint64)
+            vals = ws.get("vals", cap, torch.uint32)
+            self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
+                       _p(conic), _p(tiles), cap, _p(keys), _p(vals), st)
+        keys, vals = keys[:K], vals[:K]
         kb = sort_key_bits(T)
         skeys = ws.get("skeys", K, torch.uint64)
         svals = ws.get("svals", K, torch.uint32)
@@ -405,7 +421,7 @@ class Trainer:
                        _p(cov3d), _p(dcolors), _p(dmeans2d), _p(dconic), _p(dvs), _p(radii),
                        _p(clamped), _p(self.params), _p(self.exp_avg), _p(self.exp_avg_sq), lrs,
                        float(self.betas[0]), float(self.betas[1]), self.eps, self.step_count,
-                       int(self.bias_correction), _p(self.step_stats), st)
+                       int(self.bias_correction), _p(self.step_stats if stats is None else stats), st)
             return img
         self._call("preprocess_backward_train", L.fgs_preprocess_backward_train, C.byref(prm), _p(means), _p(self.scales), _p(self.quats), _p(self.view("rotations")),
             _p(self.opacities), _p(vm), _p(pm), _p(cp), _p(rest), _p(cov3d), _p(dcolors),
@@ -434,15 +450,16 @@ class Trainer:
         world, rank = self.world, self.rank
         mine = local_views(len(cams), world, rank)
         self.activate()
-        self.step_stats.zero_()
         scale = 1.0 / max(len(cams), 1)  # mean loss over the whole batch
         if self.fuse_adam and world == 1 and len(mine) == 1:
-            # the gradient is this one view's: Adam runs inside its backward pass
+            # the gradient is this one view's: Adam runs inside its backward
+            # pass, and the view's densification statistics go straight into
+            # the running ones (the same sums and maxima as folding them)
             self.step_count += 1
             self.render_view(cams[mine[0]], targets[mine[0]], loss_out=loss_out, loss_scale=scale,
-                             fused_adam=True)
-            fold_stats(self.stats, self.step_stats, self.n)
+                             fused_adam=True, stats=self.stats)
             return 1
+        self.step_stats.zero_()
         if not mine:
             self.grads.zero_()
         for j, v in enumerate(mine):
