@@ -1,16 +1,22 @@
 """Benchmark: FastGS training step at 1M Gaussians, 1920x1080, SH degree 3.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 3|4|5]
 
 One step = one view per GPU (weak scaling over the view batch): preprocess ->
 scan -> duplicate -> onesweep sort -> tile prep -> rasterize forward -> L1 +
 0.2 D-SSIM loss -> rasterize backward -> preprocess backward (+ activations,
-densification statistics) -> [NCCL reduce-scatter of the 59 gradient floats
-per Gaussian, sum of 3 statistics and max of the screen radius] -> Adam on
-this rank's shard of the parameters -> [NCCL all-gather of the parameters].
+densification statistics; Adam fused in on one GPU) -> [N > 1: one kernel
+reads this rank's shard of the summed gradients over NVLink multicast, applies
+Adam and writes the new parameters to every rank].
 Workload: BASELINE config 3 (seeded synthetic scene: 64-component mixture,
 seeded random target images, cameras on a radius-6 orbit). N > 1 runs under
-torchrun, one rank per GPU, NCCL; timings are the max over ranks.
+torchrun, one rank per GPU; timings are the max over ranks.
+
+--config 4 (3M Gaussians, 1600x1064, 8 views per step split over the ranks:
+strong scaling) and --config 5 (6M Gaussians, 3840x2160, forward render and
+binning sort; keys/s) print one line for those BASELINE configurations
+instead; the default line is config 3.
 
 Printed JSON (rank 0): value = views/s of the whole job with parameters,
 targets and state resident in HBM; e2e = the same step through the public API
@@ -160,6 +166,82 @@ def run_reference(args):
 _STDOUT_FD = None
 
 
+def run_other_config(args, S, Trainer, world, rank, local, dev, pg, warmup):
+    """BASELINE configs 4 (strong-scaled 8-view training step) and 5
+    (forward render + binning sort at 6M Gaussians, 4K); device-timed with
+    CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    def timed(fn, steps):
+        if pg is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for s in range(steps):
+            fn(s)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if pg is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if args.config == 4:
+        scene, cams = S.config4(0)
+        W, H = cams[0].width, cams[0].height
+        tr = Trainer(scene, dev, process_group=pg)
+        trng = np.random.default_rng(2000)
+        tg = [torch.from_numpy(trng.uniform(0, 1, (3, W * H)).astype(np.float32)).to(dev)
+              if v % world == rank else None for v in range(len(cams))]
+        for s in range(warmup):
+            tr.step(cams, tg)
+        clocks = ClockSampler(local)
+        clocks.start()
+        ms = timed(lambda s: tr.step(cams, tg), args.steps)
+        clk = clocks.stop()
+        if rank == 0:
+            views = len(cams) * args.steps
+            _emit({"metric": METRIC, "value": views / (ms / 1000.0), "unit": "views/s",
+                   "n_gpus": world, "steps": args.steps, "warmup": warmup,
+                   "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+                   "vs_baseline": None, "dtype": "f32",
+                   "data": "synthetic (seeded config-4 scene, random targets)",
+                   "config": {"workload": "config4: 3M Gaussians, 1600x1064, SH 3, 8 views per "
+                              "step sharded over the ranks, fwd+bwd+L1/D-SSIM+Adam",
+                              "global_batch": len(cams), "parallelism": f"dp{world} (view-sharded)",
+                              "gaussians": scene.n, "image": f"{W}x{H}", "exchange": tr.comm},
+                   "iters_per_s": args.steps / (ms / 1000.0),
+                   "mpix_per_s": views * W * H / (ms / 1000.0) / 1e6, "clocks": clk})
+        return 0
+    # config 5: one GPU renders; other ranks have nothing to do
+    if rank != 0:
+        return 0
+    scene, cams = S.config5(0)
+    cam = cams[0]
+    tr = Trainer(scene, dev)
+    tr.activate()
+    for _ in range(warmup):
+        tr.render_view(cam)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = timed(lambda s: tr.render_view(cam), args.steps)
+    clk = clocks.stop()
+    K = tr.last_rendered
+    P = cam.width * cam.height
+    _emit({"metric": "keys/s (forward render + binning sort) at 6M Gaussians 3840x2160",
+           "value": K * args.steps / (ms / 1000.0), "unit": "keys/s", "n_gpus": 1,
+           "steps": args.steps, "warmup": warmup, "ms_per_step": ms / args.steps,
+           "higher_is_better": True, "scaling": "none", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (seeded config-5 scene)",
+           "config": {"workload": "config5: 6M Gaussians (10% large splats), 3840x2160, SH 3, "
+                      "forward render + binning sort", "gaussians": scene.n,
+                      "image": f"{cam.width}x{cam.height}", "keys_per_view": K},
+           "mpix_per_s": P * args.steps / (ms / 1000.0) / 1e6, "clocks": clk})
+    return 0
+
+
 def _emit(line: dict) -> None:
     """Print the one JSON result line on the real standard output."""
     sys.stdout.flush()
@@ -178,6 +260,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=1_000_000, help="Gaussians (default: config 3)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5])
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -207,6 +290,8 @@ def main():
         dist.init_process_group("nccl", device_id=dev)
         pg = dist.group.WORLD
     warmup = max(3, args.warmup)
+    if args.config != 3:
+        return run_other_config(args, S, Trainer, world, rank, local, dev, pg, warmup)
 
     scene, cams = S.config3(0, n=args.n)
     n_views = max(8, world)
