@@ -70,7 +70,7 @@ __device__ __forceinline__ void splat_rows(float y, float a, float b, float c, f
 // column l % 16, rows base + l / 16 + 2k), so staged-record reads, the
 // warp-level row culling and the loop are shared by PX pixels. The per-pixel
 // arithmetic is unchanged (bit-identical results).
-template <int PX, bool kMask>
+template <int PX, bool kMask, bool kMetric>
 __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
   constexpr int kThreads = kTile / PX;
   constexpr int kWarpRows = 2 * PX;
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
     pix[k] = inside[k] ? (size_t)py * a.W + px : 0;
     pfx[k] = (float)px;
     pfy[k] = (float)py;
-    count_metric[k] = a.get_flag && inside[k] && a.metric_map[pix[k]] == 1;
+    count_metric[k] = kMetric && inside[k] && a.metric_map[pix[k]] == 1;
     T[k] = 1.0f;
     C0[k] = C1[k] = C2[k] = 0.f;
     last[k] = 0;
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
           C0[k] = fmaf(r1.z * alpha, T[k], C0[k]);
           C1[k] = fmaf(r1.w * alpha, T[k], C1[k]);
           C2[k] = fmaf(r2.x * alpha, T[k], C2[k]);
-          if (count_metric[k]) atomicAdd(a.metric_count + s_id[j], 1);
+          if (kMetric && count_metric[k]) atomicAdd(a.metric_count + s_id[j], 1);
           T[k] = test_t;
           last[k] = contributor;
           if (kMask) msk[k] |= 1u << (j & 31);  // k0 is a multiple of 32
@@ -298,10 +298,15 @@ int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
   if (p->get_flag && p->num_gaussians > 0)
     zero_i32_kernel<<<(p->num_gaussians + 255) / 256, 256, 0, s>>>(metric_count, p->num_gaussians);
   // one pixel per thread (config 3: 0.805 ms; two per thread measured 0.826 ms)
-  if (a.contrib_mask)
-    raster_fwd_kernel<1, true><<<p->num_tiles, kTile, 0, s>>>(a);
+  const dim3 grid(p->num_tiles), block(kTile);
+  if (a.contrib_mask && a.get_flag)
+    raster_fwd_kernel<1, true, true><<<grid, block, 0, s>>>(a);
+  else if (a.contrib_mask)
+    raster_fwd_kernel<1, true, false><<<grid, block, 0, s>>>(a);
+  else if (a.get_flag)
+    raster_fwd_kernel<1, false, true><<<grid, block, 0, s>>>(a);
   else
-    raster_fwd_kernel<1, false><<<p->num_tiles, kTile, 0, s>>>(a);
+    raster_fwd_kernel<1, false, false><<<grid, block, 0, s>>>(a);
   return check_launch("rasterize_forward");
 }
 
