@@ -76,9 +76,12 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
   constexpr int kWarpRows = 2 * PX;
   __shared__ float4 s_r0[kTile];  // x, y, conic.x, conic.y
   __shared__ float4 s_r1[kTile];  // conic.z, opacity, r, g
-  __shared__ float4 s_r2[kTile];  // b, exponent cut, (row lo, row hi) as int bits
+  __shared__ float4 s_r2[kTile];  // b, exponent cut, -, -
   __shared__ uint32_t s_id[kTile];
   __shared__ uint32_t s_wmax[kThreads / 32];
+  // per warp and 32-splat block of the batch: which splats can reach the
+  // warp's rows (bit j: splat 32 * block + j)
+  __shared__ uint32_t s_wmask[kThreads / 32][kTile / 32];
 
   const int tile = a.tile_order ? (int)a.tile_order[blockIdx.x] : (int)blockIdx.x;
   const int lr = threadIdx.x, lane = lr & 31;
@@ -119,6 +122,7 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
     if (__syncthreads_count(live) == 0) break;
     for (int q = lr; q < kTile; q += kThreads) {
       const int j = batch + q;
+      uint32_t bands = 0u;  // warps whose rows the splat can reach
       if (j < to_do) {
         const uint32_t g = a.point_list[range.x + j];
         const float2 xy = a.means2d[g];
@@ -127,9 +131,17 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
         splat_rows(xy.y, co.x, co.y, co.z, co.w, ty * FGS_BLOCK, rlo, rhi);
         s_r0[q] = make_float4(xy.x, xy.y, co.x, co.y);
         s_r1[q] = make_float4(co.z, co.w, a.colors[3 * (size_t)g], a.colors[3 * (size_t)g + 1]);
-        s_r2[q] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), __int_as_float(rlo),
-                              __int_as_float(rhi));
+        s_r2[q] = make_float4(a.colors[3 * (size_t)g + 2], power_cut(co.w), 0.0f, 0.0f);
         s_id[q] = g;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w)
+          if (rhi >= w * kWarpRows && rlo <= w * kWarpRows + kWarpRows - 1) bands |= 1u << w;
+      }
+      // a warp stages one whole 32-splat block per pass (kThreads is a multiple of 32)
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) {
+        const uint32_t bm = __ballot_sync(0xffffffffu, (bands >> w) & 1u);
+        if (lane == 0) s_wmask[w][q >> 5] = bm;
       }
     }
     __syncthreads();
@@ -156,11 +168,10 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
       uint32_t msk[PX];
 #pragma unroll
       for (int k = 0; k < PX; ++k) msk[k] = 0u;
-      const int kend = min(k0 + 32, cnt);
-      for (int j = k0; j < kend; ++j) {
+      // walk only the block's splats that can reach this warp's rows, in order
+      for (uint32_t wm = s_wmask[lr >> 5][k0 >> 5]; wm != 0u; wm &= wm - 1u) {
+        const int j = k0 + __ffs(wm) - 1;
         const float4 r2 = s_r2[j];
-        // warp-uniform: the splat cannot reach this warp's rows
-        if (__float_as_int(r2.w) < wrow || __float_as_int(r2.z) > wrow + kWarpRows - 1) continue;
         const float4 r0 = s_r0[j];
         const float4 r1 = s_r1[j];
         // the reference counts every splat it steps over (fastgs_rasterize.metal:99)

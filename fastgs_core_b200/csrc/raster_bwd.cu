@@ -275,19 +275,23 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
 #pragma unroll
     for (int k = 0; k < PX; ++k) mor |= msk[k];
     const int sbase = 32 * s_blocal[bi];
-    for (int jj = 0; jj < cnt; ++jj) {
+    // the bucket's splats to walk; with the mask, only those that contributed
+    // to one of this warp's pixels (warp-uniform)
+    uint32_t todo = cnt == 32 ? 0xffffffffu : ((1u << cnt) - 1u);
+    if constexpr (kMask) todo &= __reduce_or_sync(0xffffffffu, mor);
+    for (; todo != 0u; todo &= todo - 1u) {
+      const int jj = __ffs(todo) - 1;
       const int j = 32 * bi + jj;  // staged record
       const int s = sbase + jj;    // splat index within the tile
       bool v[PX], vg[PX];
       float dx[PX], dy[PX], G[PX], oG[PX], alpha[PX];
       float4 r0, r1, r2;
       if constexpr (kMask) {
-        // the forward pass recorded which pairs contributed: skip the splat
-        // when none of this warp's pairs did (warp-uniform), else evaluate
-        // the exponential with the fast intrinsic, except close to the 0.99
-        // clamp, whose side decides whether G receives a gradient and is
-        // therefore taken from the forward pass's exact arithmetic
-        if (__ballot_sync(0xffffffffu, (mor >> jj) & 1u) == 0u) continue;
+        // the forward pass recorded which pairs contributed (the walk skips
+        // splats none of this warp's pairs took part in); the exponential is
+        // the fast intrinsic, except close to the 0.99 clamp, whose side
+        // decides whether G receives a gradient and is therefore taken from
+        // the forward pass's exact arithmetic
         r0 = s_r0[j];
         r1 = s_r1[j];
         r2 = s_r2[j];
