@@ -190,9 +190,12 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
             done[k] = true;
             continue;
           }
-          C0[k] = fmaf(r1.z * alpha, T[k], C0[k]);
-          C1[k] = fmaf(r1.w * alpha, T[k], C1[k]);
-          C2[k] = fmaf(r2.x * alpha, T[k], C2[k]);
+          // one weight per pair, fused accumulation (the CPU checker's
+          // definition: c = fma(col, alpha * T, c))
+          const float wgt = alpha * T[k];
+          C0[k] = fmaf(r1.z, wgt, C0[k]);
+          C1[k] = fmaf(r1.w, wgt, C1[k]);
+          C2[k] = fmaf(r2.x, wgt, C2[k]);
           if (kMetric && count_metric[k]) atomicAdd(a.metric_count + s_id[j], 1);
           T[k] = test_t;
           last[k] = contributor;

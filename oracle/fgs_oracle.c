@@ -115,13 +115,15 @@ static inline float fgs_logf(float x) {
 #ifdef FGS_ORACLE_LIBM
 #define O_EXP(x) expf(x)
 #define O_LOG(x) logf(x)
-/* colour accumulation c += (col * alpha) * T as two rounded ops */
-#define O_ACC(c, ca, t) ((c) + (ca) * (t))
+/* colour accumulation c += (col * alpha) * T as rounded ops, in the
+   reference's order (fastgs_rasterize.metal:122) */
+#define O_ACC(c, col, alpha, t) ((c) + ((col) * (alpha)) * (t))
 #else
 #define O_EXP(x) fgs_expf(x)
 #define O_LOG(x) fgs_logf(x)
-/* the CUDA kernels fuse the colour accumulation: c = fma(col * alpha, T, c) */
-#define O_ACC(c, ca, t) fmaf((ca), (t), (c))
+/* the CUDA kernels weight once per pair and fuse the accumulation:
+   w = alpha * T (rounded), c = fma(col, w, c) */
+#define O_ACC(c, col, alpha, t) fmaf((col), (alpha) * (t), (c))
 #endif
 
 static inline float fmin_t(float a, float b) { return b < a ? b : a; }
@@ -630,7 +632,7 @@ void o_render_forward(int W, int H, int get_flag, const uint32_t* ranges,
           if (alpha < 1.0f / 255.0f) continue;
           const float test_t = T * (1.0f - alpha);
           if (test_t < 0.0001f) break;
-          for (int ch = 0; ch < 3; ++ch) C[ch] = O_ACC(C[ch], colors[3 * (size_t)g + ch] * alpha, T);
+          for (int ch = 0; ch < 3; ++ch) C[ch] = O_ACC(C[ch], colors[3 * (size_t)g + ch], alpha, T);
           if (get_flag && metric_map[pix] == 1) {
 #pragma omp atomic
             metric_count[g] += 1;
