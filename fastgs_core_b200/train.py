@@ -219,6 +219,9 @@ class Trainer:
         # forward pass records contributing pairs for the backward pass
         self.contrib_mask = os.environ.get("FGS_CONTRIB_MASK", "1") != "0"
         self._key_cap = 0  # capacity of the grow-only key buffers
+        self._k_ready = torch.cuda.Event()  # recorded after each view's key-count copy
+        self._scan_done = torch.cuda.Event()
+        self._k_stream = torch.cuda.Stream(device=self.dev)
         # one view on one rank: Adam fused into the backward pass (no
         # gradient buffer round trip); the gradient buffer is then not written
         self.fuse_adam = os.environ.get("FGS_FUSE_ADAM", "1") != "0"
@@ -326,44 +329,55 @@ class Trainer:
         self._call("preprocess", L.fgs_preprocess_forward, C.byref(prm), _p(means), _p(dc), _p(rest), None, _p(self.opacities), _p(self.scales),
             _p(self.quats), None, _p(vm), _p(pm), _p(cp), _p(vs_in), _p(radii), _p(xys), _p(depths),
             _p(cov3d), _p(rgb), _p(conic), _p(tiles), _p(clamped), _p(vs_out), st)
+        cap = self._key_cap
+        kb = sort_key_bits(T)
+
+        def key_buffers(c):
+            # keys, values, sorted keys and values, sort workspace for c keys
+            # (the workspace for c keys serves any count up to c)
+            sws_n = int(L.fgs_sort_workspace_bytes(c, kb))
+            bufs = (ws.get("keys", c, torch.uint64), ws.get("vals", c, torch.uint32),
+                    ws.get("skeys", c, torch.uint64), ws.get("svals", c, torch.uint32),
+                    ws.get("sort_ws", sws_n, torch.uint8))
+            return [_p(t) for t in bufs], sws_n, bufs
+
+        if cap > 0:
+            kp, sws_n, kbufs = key_buffers(cap)  # prepared before the scan: nothing waits on it
         offsets = ws.get("offsets", n, torch.uint32)
         total = ws.get("total", 1, torch.uint64)
         scan_scr = ws.get("scan_scr", int(L.fgs_scan_scratch_bytes(n)), torch.uint8)
         self._call("scan", L.fgs_inclusive_scan_u32, n, _p(tiles), _p(offsets), _p(total), _p(scan_scr), st)
-        self.k_host.copy_(total, non_blocking=True)
-        k_ready = torch.cuda.Event()
-        k_ready.record(torch.cuda.current_stream(d))
+        # the 8-byte count goes to the host on a side stream, so that the copy
+        # does not sit between the scan and the next launch on this stream
+        cur = torch.cuda.current_stream(d)
+        self._scan_done.record(cur)
+        with torch.cuda.stream(self._k_stream):
+            self._k_stream.wait_event(self._scan_done)
+            self.k_host.copy_(total, non_blocking=True)
+            self._k_ready.record(self._k_stream)
+        k_ready = self._k_ready
         # Duplicate-with-keys runs before the host knows K, into grow-only
         # buffers of the capacity the previous views needed (its writes stop at
         # the capacity); the host only waits for the count, and repeats the
         # launch with larger buffers in the rare view that outgrows them.
-        cap = self._key_cap
         if cap > 0:
-            keys = ws.get("keys", cap, torch.uint64)
-            vals = ws.get("vals", cap, torch.uint32)
             self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
-                       _p(conic), _p(tiles), cap, _p(keys), _p(vals), st)
+                       _p(conic), _p(tiles), cap, kp[0], kp[1], st)
         k_ready.synchronize()  # the one host sync: K sizes the sort and the bucket arrays
         K = int(self.k_host.item())
         self.last_rendered = K
+        if K > cap:
+            cap = self._key_cap = K + K // 4 + 1024
+            kp, sws_n, kbufs = key_buffers(cap)
+            self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
+                       _p(conic), _p(tiles), cap, kp[0], kp[1], st)
+        if K > 0:
+            self._call("sort", L.fgs_sort_pairs, K, kb, *kp, sws_n, st)
         img = ws.get("img", 3 * P, torch.float32)
         if K == 0:
             img.view(3, P).copy_(self.background.view(3, 1).expand(3, P))
             return img
-        if K > cap:
-            cap = self._key_cap = K + K // 4 + 1024
-            keys = ws.get("keys", cap, torch.uint64)
-            vals = ws.get("vals", cap, torch.uint32)
-            self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
-                       _p(conic), _p(tiles), cap, _p(keys), _p(vals), st)
-        keys, vals = keys[:K], vals[:K]
-        kb = sort_key_bits(T)
-        skeys = ws.get("skeys", K, torch.uint64)
-        svals = ws.get("svals", K, torch.uint32)
-        sws_n = int(L.fgs_sort_workspace_bytes(K, kb))
-        sws = ws.get("sort_ws", sws_n, torch.uint8)
-        self._call("sort", L.fgs_sort_pairs, K, kb, _p(keys), _p(vals), _p(skeys), _p(svals), _p(sws),
-                   sws_n, st)
+        skeys, svals = kbufs[2][:K], kbufs[3][:K]
         self.launches += 2 + (kb + 7) // 8  # histogram, digit scan, one onesweep pass per digit
         ranges = ws.get("ranges", 2 * T, torch.uint32)
         bcount = ws.get("bcount", T, torch.uint32)
