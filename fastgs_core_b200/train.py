@@ -221,7 +221,11 @@ class Trainer:
         self._key_cap = 0  # capacity of the grow-only key buffers
         self._k_ready = torch.cuda.Event()  # recorded after each view's key-count copy
         self._scan_done = torch.cuda.Event()
+        self._cam_ready = torch.cuda.Event()
+        self._g2_ready = torch.cuda.Event()
         self._k_stream = torch.cuda.Stream(device=self.dev)
+        self._cam_host = torch.empty(35, dtype=torch.float32, pin_memory=True)
+        self._views = 0
         # one view on one rank: Adam fused into the backward pass (no
         # gradient buffer round trip); the gradient buffer is then not written
         self.fuse_adam = os.environ.get("FGS_FUSE_ADAM", "1") != "0"
@@ -297,17 +301,23 @@ class Trainer:
         gx, gy = tile_grid(W, H)
         T = gx * gy
         st = self._stream()
-        cm = ws.get("cam", 35, torch.float32)
-        # pinned staging: the previous view's copy has completed by now (each
-        # view synchronises once on its key count)
-        if not hasattr(self, "_cam_host"):
-            self._cam_host = torch.empty(35, dtype=torch.float32, pin_memory=True)
+        # camera upload on the side stream into one of two device slots: the
+        # slot's previous user (two views back) and the pinned staging's last
+        # copy are complete, because the host has since waited on a later
+        # view's key count, which that stream orders after them
+        cm = ws.get("cam%d" % (self._views % 2), 35, torch.float32)
+        self._views += 1
         hc = self._cam_host.numpy()
         hc[0:16] = cam.viewmatrix.reshape(-1)
         hc[16:32] = cam.projmatrix.reshape(-1)
         hc[32:35] = cam.campos.reshape(-1)
-        cm.copy_(self._cam_host, non_blocking=True)
+        cur = torch.cuda.current_stream(d)
+        with torch.cuda.stream(self._k_stream):
+            cm.copy_(self._cam_host, non_blocking=True)
+            self._cam_ready.record(self._k_stream)
+        cur.wait_event(self._cam_ready)
         vm, pm, cp = cm[0:16], cm[16:32], cm[32:35]
+        self.last_cam = cm  # [view 16 | projection 16 | position 3] of this view
         prm = PreprocessParams(n, self.sh_degree, 15, 1.0, 1.0, float(cam.tan_fovx), float(cam.tan_fovy),
                                W, H, 0, 0)
         means = self.view("means3d")
@@ -349,7 +359,6 @@ class Trainer:
         self._call("scan", L.fgs_inclusive_scan_u32, n, _p(tiles), _p(offsets), _p(total), _p(scan_scr), st)
         # the 8-byte count goes to the host on a side stream, so that the copy
         # does not sit between the scan and the next launch on this stream
-        cur = torch.cuda.current_stream(d)
         self._scan_done.record(cur)
         with torch.cuda.stream(self._k_stream):
             self._k_stream.wait_event(self._scan_done)
@@ -373,6 +382,16 @@ class Trainer:
                        _p(conic), _p(tiles), cap, kp[0], kp[1], st)
         if K > 0:
             self._call("sort", L.fgs_sort_pairs, K, kb, *kp, sws_n, st)
+        if target is not None:
+            # the raster-gradient accumulators are zeroed on the side stream
+            # while this stream sorts and renders (every earlier use of them
+            # finished before this view's scan, which the host just saw)
+            o1 = -(-2 * n // 4) * 4
+            o2 = o1 + -(-3 * n // 4) * 4
+            g2 = ws.get("g_raster", o2 + 8 * n, torch.float32)
+            with torch.cuda.stream(self._k_stream):
+                g2.zero_()
+                self._g2_ready.record(self._k_stream)
         img = ws.get("img", 3 * P, torch.float32)
         if K == 0:
             img.view(3, P).copy_(self.background.view(3, 1).expand(3, P))
@@ -417,10 +436,7 @@ class Trainer:
         # backward
         # one zeroed buffer, each part starting on a 16-byte boundary (the
         # kernels read the conic and viewspace gradients as float4)
-        o1 = -(-2 * n // 4) * 4
-        o2 = o1 + -(-3 * n // 4) * 4
-        g2 = ws.get("g_raster", o2 + 8 * n, torch.float32)
-        g2.zero_()
+        cur.wait_event(self._g2_ready)
         dmeans2d, dcolors = g2[:2 * n], g2[o1:o1 + 3 * n]
         dconic, dvs = g2[o2:o2 + 4 * n], g2[o2 + 4 * n:o2 + 8 * n]
         self.raster_grads = (dmeans2d, dcolors, dconic, dvs)

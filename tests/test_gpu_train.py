@@ -209,7 +209,7 @@ def test_adam_fused_into_backward_matches_separate(cuda_dev):
     tr.render_view(cam, target)  # leaves this view's backward inputs in the workspace
     torch.cuda.synchronize()
     ws = tr.ws.b
-    cm = ws["cam"][:35]
+    cm = tr.last_cam
     gm, gc, gk, gv = tr.raster_grads
     prm = PreprocessParams(n, 3, 15, 1.0, 1.0, float(cam.tan_fovx), float(cam.tan_fovy), 80, 48, 0, 0)
     p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
