@@ -24,17 +24,20 @@ namespace fgs {
 // ---------------------------------------------------------------- duplicate
 constexpr int kDupThreads = 256;
 
+// Thread j emits the keys of Gaussian i = order[j] (order == NULL: i = j) at
+// the offsets of the inclusive scan `offsets` taken in that order.
 __global__ void __launch_bounds__(kDupThreads)
     duplicate_kernel(int n, float mult, int gx, int gy, const float2* __restrict__ xys,
-                     const float* __restrict__ depths, const uint32_t* __restrict__ offsets,
-                     const float4* __restrict__ conic, const uint32_t* __restrict__ tiles,
-                     int64_t num_rendered, uint64_t* __restrict__ keys,
-                     uint32_t* __restrict__ values) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+                     const float* __restrict__ depths, const uint32_t* __restrict__ order,
+                     const uint32_t* __restrict__ offsets, const float4* __restrict__ conic,
+                     const uint32_t* __restrict__ tiles, int64_t num_rendered,
+                     uint64_t* __restrict__ keys, uint32_t* __restrict__ values) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  const int i = order ? (int)order[j] : j;
   const uint32_t cnt = tiles[i];
   if (cnt == 0u) return;
-  const int64_t off0 = (i == 0) ? 0 : (int64_t)offsets[i - 1];
+  const int64_t off0 = (j == 0) ? 0 : (int64_t)offsets[j - 1];
   const uint64_t dbits = (uint64_t)__float_as_uint(depths[i]);
   const float2 p = xys[i];
   int64_t off = off0;
@@ -54,6 +57,22 @@ __global__ void __launch_bounds__(kDupThreads)
   }
 }
 
+// The depth-first ordering of the training path: (depth bits, index) pairs of
+// every Gaussian, then the per-position tile counts in the sorted order.
+__global__ void depth_keys_kernel(int n, const float* __restrict__ depths,
+                                  uint64_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  keys[i] = (uint64_t)__float_as_uint(depths[i]);
+  vals[i] = (uint32_t)i;
+}
+
+__global__ void gather_u32_kernel(int n, const uint32_t* __restrict__ src,
+                                  const uint32_t* __restrict__ index, uint32_t* __restrict__ dst) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j < n) dst[j] = src[index[j]];
+}
+
 // --------------------------------------------------------------------- sort
 constexpr int kRadix = 256;
 constexpr int kSortThreads = 256;
@@ -65,10 +84,11 @@ constexpr uint32_t kFlagAgg = 1u << 30;
 constexpr uint32_t kFlagPrefix = 2u << 30;
 constexpr uint32_t kValueMask = (1u << 30) - 1u;
 constexpr int kSpinLimit = 1 << 22;
+constexpr int kLookWindow = 8;  // predecessors read per look-back round trip
 constexpr int kSortDynSmem = kPart * (8 + 4);
 
 __global__ void __launch_bounds__(256)
-    sort_histogram_kernel(const uint64_t* __restrict__ keys, int64_t n, int passes,
+    sort_histogram_kernel(const uint64_t* __restrict__ keys, int64_t n, int bit0, int passes,
                           uint32_t* __restrict__ hist) {
   __shared__ uint32_t s_h[kMaxPasses][kRadix];
   for (int k = threadIdx.x; k < kMaxPasses * kRadix; k += blockDim.x) (&s_h[0][0])[k] = 0u;
@@ -76,7 +96,7 @@ __global__ void __launch_bounds__(256)
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     const uint64_t k = keys[i];
-    for (int p = 0; p < passes; ++p) atomicAdd(&s_h[p][(k >> (8 * p)) & 0xffu], 1u);
+    for (int p = 0; p < passes; ++p) atomicAdd(&s_h[p][(k >> (bit0 + 8 * p)) & 0xffu], 1u);
   }
   __syncthreads();
   for (int k = threadIdx.x; k < passes * kRadix; k += blockDim.x) {
@@ -194,25 +214,43 @@ __global__ void __launch_bounds__(kSortThreads)
     for (int ww = 0; ww < w; ++ww) add += s_wsum[ww];
     s_local_start[d] = x - cnt + add;
   }
-  // decoupled look-back over earlier partitions for digit d
+  // decoupled look-back over earlier partitions for digit d, reading a window
+  // of kLookWindow predecessors per round trip: their values are summed from
+  // the nearest one down until an inclusive prefix is met; a predecessor that
+  // has published nothing yet ends the round, and the next window starts there
   uint32_t excl = 0;
   if (part > 0) {
     int64_t j = (int64_t)part - 1;
     int spins = 0;
     while (j >= 0) {
-      const uint32_t s = ld_volatile(lookback + (size_t)j * kRadix + d);
-      const uint32_t flag = s & ~kValueMask;
-      if (flag == 0u) {
+      uint32_t sv[kLookWindow];
+#pragma unroll
+      for (int u = 0; u < kLookWindow; ++u)
+        sv[u] = (j - u >= 0) ? ld_volatile(lookback + (size_t)(j - u) * kRadix + d) : 0u;
+      bool found = false;
+      int used = 0;
+#pragma unroll
+      for (int u = 0; u < kLookWindow; ++u) {
+        if (j - u < 0) break;
+        const uint32_t flag = sv[u] & ~kValueMask;
+        if (flag == 0u) break;
+        excl += sv[u] & kValueMask;
+        ++used;
+        if (flag == kFlagPrefix) {
+          found = true;
+          break;
+        }
+      }
+      if (found) break;
+      j -= used;
+      if (used < kLookWindow && j >= 0) {
+        // the predecessor at j has published nothing yet: wait and re-read
         if (++spins > kSpinLimit) {
           atomicExch(err, 1);
           break;
         }
         __nanosleep(32);
-        continue;
       }
-      excl += s & kValueMask;
-      if (flag == kFlagPrefix) break;
-      --j;
     }
     st_volatile(lb, kFlagPrefix | ((excl + real_cnt) & kValueMask));
   }
@@ -372,9 +410,29 @@ int fgs_duplicate_with_keys(int32_t n, float mult, int32_t tile_bounds_x, int32_
                 "xys must be 8-byte, conic_opacity 16-byte aligned");
   FGS_CHECK_ARG(tile_bounds_x > 0 && tile_bounds_y > 0, "tile bounds must be positive");
   duplicate_kernel<<<(n + kDupThreads - 1) / kDupThreads, kDupThreads, 0, (cudaStream_t)stream>>>(
-      n, mult, tile_bounds_x, tile_bounds_y, (const float2*)xys, depths, point_offsets,
+      n, mult, tile_bounds_x, tile_bounds_y, (const float2*)xys, depths, nullptr, point_offsets,
       (const float4*)conic_opacity, tiles_touched, num_rendered, keys_unsorted, values_unsorted);
   return check_launch("duplicate_with_keys");
+}
+
+int fgs_duplicate_with_keys_ordered(int32_t n, float mult, int32_t tile_bounds_x,
+                                    int32_t tile_bounds_y, const float* xys, const float* depths,
+                                    const uint32_t* order, const uint32_t* offsets_in_order,
+                                    const float* conic_opacity, const uint32_t* tiles_touched,
+                                    int64_t num_rendered, uint64_t* keys, uint32_t* values,
+                                    void* stream) {
+  FGS_CHECK_ARG(n >= 0 && num_rendered >= 0, "sizes must be >= 0");
+  if (n == 0 || num_rendered == 0) return FGS_OK;
+  FGS_CHECK_ARG(xys && depths && order && offsets_in_order && conic_opacity && tiles_touched &&
+                    keys && values,
+                "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(xys, 8) && FGS_ALIGNED(conic_opacity, 16),
+                "xys must be 8-byte, conic_opacity 16-byte aligned");
+  FGS_CHECK_ARG(tile_bounds_x > 0 && tile_bounds_y > 0, "tile bounds must be positive");
+  duplicate_kernel<<<(n + kDupThreads - 1) / kDupThreads, kDupThreads, 0, (cudaStream_t)stream>>>(
+      n, mult, tile_bounds_x, tile_bounds_y, (const float2*)xys, depths, order, offsets_in_order,
+      (const float4*)conic_opacity, tiles_touched, num_rendered, keys, values);
+  return check_launch("duplicate_with_keys_ordered");
 }
 
 size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits) {
@@ -393,8 +451,18 @@ size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits) {
 int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,
                    const uint32_t* values_in, uint64_t* keys_out, uint32_t* values_out,
                    void* workspace, size_t workspace_bytes, void* stream) {
+  return fgs_sort_pairs_bits(num_rendered, 0, key_bits, keys_in, values_in, keys_out, values_out,
+                             workspace, workspace_bytes, stream);
+}
+
+int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end,
+                        const uint64_t* keys_in, const uint32_t* values_in, uint64_t* keys_out,
+                        uint32_t* values_out, void* workspace, size_t workspace_bytes,
+                        void* stream) {
   FGS_CHECK_ARG(num_rendered >= 0, "num_rendered must be >= 0");
-  FGS_CHECK_ARG(key_bits >= 1 && key_bits <= 64, "key_bits must be in [1, 64]");
+  FGS_CHECK_ARG(bit_begin >= 0 && bit_end > bit_begin && bit_end <= 64,
+                "need 0 <= bit_begin < bit_end <= 64");
+  const int32_t key_bits = bit_end - bit_begin;
   if (num_rendered == 0) return FGS_OK;
   if (num_rendered > (int64_t)kValueMask) {
     fgs::set_error("sort supports at most %u keys, got %lld", kValueMask, (long long)num_rendered);
@@ -428,7 +496,8 @@ int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t hb = (num_rendered + 4095) / 4096;
   const int hblocks = (int)(hb < (int64_t)sms * 4 ? hb : (int64_t)sms * 4);
-  sort_histogram_kernel<<<hblocks > 0 ? hblocks : 1, 256, 0, s>>>(keys_in, num_rendered, passes, hist);
+  sort_histogram_kernel<<<hblocks > 0 ? hblocks : 1, 256, 0, s>>>(keys_in, num_rendered, bit_begin,
+                                                                  passes, hist);
   sort_hist_scan_kernel<<<passes, kRadix, 0, s>>>(hist);
   const uint64_t* src_k = keys_in;
   const uint32_t* src_v = values_in;
@@ -438,12 +507,40 @@ int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_
     uint64_t* dk = to_out ? keys_out : tmp_keys;
     uint32_t* dv = to_out ? values_out : tmp_vals;
     onesweep_kernel<<<(unsigned)parts, kSortThreads, kSortDynSmem, s>>>(
-        src_k, src_v, dk, dv, num_rendered, 8 * p, hist + p * kRadix,
+        src_k, src_v, dk, dv, num_rendered, bit_begin + 8 * p, hist + p * kRadix,
         lookback + (size_t)p * parts * kRadix, counters + p, err);
     src_k = dk;
     src_v = dv;
   }
   return check_launch("sort_pairs");
+}
+
+size_t fgs_depth_order_workspace_bytes(int32_t n) {
+  const int64_t m = n > 0 ? n : 1;
+  return align256((size_t)m * 8) * 2 + align256((size_t)m * 4) + fgs_sort_workspace_bytes(m, 32);
+}
+
+int fgs_depth_order(int32_t n, const float* depths, const uint32_t* tiles_touched, uint32_t* order,
+                    uint32_t* tiles_in_order, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  FGS_CHECK_ARG(n >= 0, "n must be >= 0");
+  if (n == 0) return FGS_OK;
+  FGS_CHECK_ARG(depths && tiles_touched && order && tiles_in_order && workspace, "missing pointer");
+  FGS_CHECK_ARG(workspace_bytes >= fgs_depth_order_workspace_bytes(n), "depth order workspace too small");
+  char* w = (char*)workspace;
+  uint64_t* keys = (uint64_t*)w;
+  w += align256((size_t)n * 8);
+  uint64_t* skeys = (uint64_t*)w;
+  w += align256((size_t)n * 8);
+  uint32_t* vals = (uint32_t*)w;
+  w += align256((size_t)n * 4);
+  const size_t sws = fgs_sort_workspace_bytes(n, 32);
+  cudaStream_t s = (cudaStream_t)stream;
+  depth_keys_kernel<<<(n + 255) / 256, 256, 0, s>>>(n, depths, keys, vals);
+  int st = fgs_sort_pairs_bits(n, 0, 32, keys, vals, skeys, order, w, sws, stream);
+  if (st) return st;
+  gather_u32_kernel<<<(n + 255) / 256, 256, 0, s>>>(n, tiles_touched, order, tiles_in_order);
+  return check_launch("depth_order");
 }
 
 int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorted_keys,

@@ -219,6 +219,7 @@ class Trainer:
         # forward pass records contributing pairs for the backward pass
         self.contrib_mask = os.environ.get("FGS_CONTRIB_MASK", "1") != "0"
         self._key_cap = 0  # capacity of the grow-only key buffers
+        self.depth_first = os.environ.get("FGS_DEPTH_FIRST", "1") != "0"
         self._k_ready = torch.cuda.Event()  # recorded after each view's key-count copy
         self._scan_done = torch.cuda.Event()
         self._cam_ready = torch.cuda.Event()
@@ -233,7 +234,7 @@ class Trainer:
         self.launches = 0
 
     # kernels each C entry point launches (memsets are not kernels)
-    _KERNELS = {"preprocess": 1, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
+    _KERNELS = {"preprocess": 1, "depth_order": 8, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
                 "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1,
                 "preprocess_backward_adam": 1, "activate": 1,
                 "adam": 1}
@@ -341,11 +342,15 @@ class Trainer:
             _p(cov3d), _p(rgb), _p(conic), _p(tiles), _p(clamped), _p(vs_out), st)
         cap = self._key_cap
         kb = sort_key_bits(T)
+        # depth-first binning: order the Gaussians by depth, emit keys in that
+        # order, then sort only the tile bits of the K keys (same result as
+        # sorting all bits of keys emitted in index order)
+        sort_lo = 32 if self.depth_first else 0
 
         def key_buffers(c):
             # keys, values, sorted keys and values, sort workspace for c keys
             # (the workspace for c keys serves any count up to c)
-            sws_n = int(L.fgs_sort_workspace_bytes(c, kb))
+            sws_n = int(L.fgs_sort_workspace_bytes(c, kb - sort_lo))
             bufs = (ws.get("keys", c, torch.uint64), ws.get("vals", c, torch.uint32),
                     ws.get("skeys", c, torch.uint64), ws.get("svals", c, torch.uint32),
                     ws.get("sort_ws", sws_n, torch.uint8))
@@ -356,7 +361,16 @@ class Trainer:
         offsets = ws.get("offsets", n, torch.uint32)
         total = ws.get("total", 1, torch.uint64)
         scan_scr = ws.get("scan_scr", int(L.fgs_scan_scratch_bytes(n)), torch.uint8)
-        self._call("scan", L.fgs_inclusive_scan_u32, n, _p(tiles), _p(offsets), _p(total), _p(scan_scr), st)
+        order = None
+        scan_in = tiles
+        if self.depth_first:
+            order = ws.get("depth_order", n, torch.uint32)
+            scan_in = ws.get("tiles_in_order", n, torch.uint32)
+            dws_n = int(L.fgs_depth_order_workspace_bytes(n))
+            dws = ws.get("depth_order_ws", dws_n, torch.uint8)
+            self._call("depth_order", L.fgs_depth_order, n, _p(depths), _p(tiles), _p(order), _p(scan_in),
+                       _p(dws), dws_n, st)
+        self._call("scan", L.fgs_inclusive_scan_u32, n, _p(scan_in), _p(offsets), _p(total), _p(scan_scr), st)
         # the 8-byte count goes to the host on a side stream, so that the copy
         # does not sit between the scan and the next launch on this stream
         self._scan_done.record(cur)
@@ -369,19 +383,25 @@ class Trainer:
         # buffers of the capacity the previous views needed (its writes stop at
         # the capacity); the host only waits for the count, and repeats the
         # launch with larger buffers in the rare view that outgrows them.
+        def dup(c, kp):
+            if order is None:
+                self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths),
+                           _p(offsets), _p(conic), _p(tiles), c, kp[0], kp[1], st)
+            else:
+                self._call("duplicate", L.fgs_duplicate_with_keys_ordered, n, 1.0, gx, gy, _p(xys),
+                           _p(depths), _p(order), _p(offsets), _p(conic), _p(tiles), c, kp[0], kp[1], st)
+
         if cap > 0:
-            self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
-                       _p(conic), _p(tiles), cap, kp[0], kp[1], st)
+            dup(cap, kp)
         k_ready.synchronize()  # the one host sync: K sizes the sort and the bucket arrays
         K = int(self.k_host.item())
         self.last_rendered = K
         if K > cap:
             cap = self._key_cap = K + K // 4 + 1024
             kp, sws_n, kbufs = key_buffers(cap)
-            self._call("duplicate", L.fgs_duplicate_with_keys, n, 1.0, gx, gy, _p(xys), _p(depths), _p(offsets),
-                       _p(conic), _p(tiles), cap, kp[0], kp[1], st)
+            dup(cap, kp)
         if K > 0:
-            self._call("sort", L.fgs_sort_pairs, K, kb, *kp, sws_n, st)
+            self._call("sort", L.fgs_sort_pairs_bits, K, sort_lo, kb, *kp, sws_n, st)
         if target is not None:
             # the raster-gradient accumulators are zeroed on the side stream
             # while this stream sorts and renders (every earlier use of them
@@ -397,7 +417,8 @@ class Trainer:
             img.view(3, P).copy_(self.background.view(3, 1).expand(3, P))
             return img
         skeys, svals = kbufs[2][:K], kbufs[3][:K]
-        self.launches += 2 + (kb + 7) // 8  # histogram, digit scan, one onesweep pass per digit
+        self.last_sorted = (skeys, svals)
+        self.launches += 2 + (kb - sort_lo + 7) // 8  # histogram, digit scan, one pass per digit
         ranges = ws.get("ranges", 2 * T, torch.uint32)
         bcount = ws.get("bcount", T, torch.uint32)
         boffs = ws.get("boffs", T, torch.uint32)

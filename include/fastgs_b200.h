@@ -131,6 +131,38 @@ FGS_API int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_
                    const uint32_t* values_in, uint64_t* keys_out, uint32_t* values_out,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* As fgs_sort_pairs on key bits [bit_begin, bit_end) only (stable: pairs
+ * with equal bits there keep their input order). The workspace is
+ * fgs_sort_workspace_bytes(num_rendered, bit_end - bit_begin). */
+FGS_API int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end,
+                                const uint64_t* keys_in, const uint32_t* values_in,
+                                uint64_t* keys_out, uint32_t* values_out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* Depth-first binning, the training path's replacement for sorting the K
+ * duplicated (tile | depth) keys on all 32 + ceil(log2 T) bits: the n
+ * Gaussians are ordered by depth (stable, so equal depths keep index order),
+ * fgs_duplicate_with_keys_ordered emits the keys in that order, and a stable
+ * sort of the tile bits [32, 32 + ceil(log2 T)) alone then yields the same
+ * sorted keys and values as fgs_sort_pairs on the Gaussian-order keys: within
+ * a tile, depth order with ties in index order. No reference counterpart
+ * (fastgs_core/binding/binding.cpp:186-197 duplicates, then sorts all bits).
+ *
+ * fgs_depth_order writes order[n] (Gaussian indices by depth) and
+ * tiles_in_order[j] = tiles_touched[order[j]]; the caller scans the latter
+ * (fgs_inclusive_scan_u32) for the offsets in order. */
+FGS_API size_t fgs_depth_order_workspace_bytes(int32_t n);
+FGS_API int fgs_depth_order(int32_t n, const float* depths, const uint32_t* tiles_touched,
+                            uint32_t* order, uint32_t* tiles_in_order, void* workspace,
+                            size_t workspace_bytes, void* stream);
+FGS_API int fgs_duplicate_with_keys_ordered(int32_t n, float mult, int32_t tile_bounds_x,
+                                            int32_t tile_bounds_y, const float* xys,
+                                            const float* depths, const uint32_t* order,
+                                            const uint32_t* offsets_in_order,
+                                            const float* conic_opacity,
+                                            const uint32_t* tiles_touched, int64_t num_rendered,
+                                            uint64_t* keys, uint32_t* values, void* stream);
+
 /* ---------------------------------------------------------------------------
  * fgs_sort_pairs without any allocation. No counterpart in the reference: it
  * exists for callers that cannot allocate device memory when they sort (a

@@ -259,3 +259,24 @@ def test_trainer_fused_adam_step(cuda_dev):
     assert a.step_count == b.step_count == 3
     assert rel_err((a.params - p0).cpu().numpy(), (b.params - p0).cpu().numpy()) < 1e-3
     assert rel_err(a.stats.cpu().numpy(), b.stats.cpu().numpy()) < 1e-3
+
+
+@pytest.mark.parametrize("n", [3000, 20_001])
+def test_depth_first_binning_matches_full_sort(n, cuda_dev):
+    """Depth-first binning (order Gaussians by depth, emit keys in that order,
+    sort the tile bits only) gives the sorted keys and values of the full
+    64-bit sort of index-order keys, bit for bit, and so the same image."""
+    scene, cam = S.small_scene(40 + n % 7, n, 3, 160, 96, log_scale_mu=-3.0)
+    out = []
+    for depth_first in (True, False):
+        tr = Trainer(scene, cuda_dev)
+        tr.depth_first = depth_first
+        tr.activate()
+        img = tr.render_view(cam).clone()
+        k, v = tr.last_sorted
+        out.append((k.clone(), v.clone(), img))
+    (k1, v1, i1), (k2, v2, i2) = out
+    assert k1.numel() > 0
+    assert torch.equal(k1, k2)
+    assert torch.equal(v1, v2)
+    assert torch.equal(i1, i2)
