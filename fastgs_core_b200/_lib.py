@@ -54,9 +54,10 @@ _SIGS = {
     "fgs_rasterize_backward": (C.c_int, [C.POINTER(RasterParams)] + [_p] * 20),
     "fgs_preprocess_backward": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 24),
     "fgs_activate_params": (C.c_int, [_i64, _p, _p, _p, _p, _p]),
-    "fgs_preprocess_backward_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 16
+    "fgs_preprocess_backward_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 11
                                       + [_i32, _p, _p, _p]),
-    "fgs_preprocess_backward_adam": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 17
+    "fgs_preprocess_forward_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 15),
+    "fgs_preprocess_backward_adam": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 14
                                      + [_f, _f, _f, _i32, _i32, _p, _p]),
     "fgs_loss_scratch_bytes": (_sz, [_i32, _i32]),
     "fgs_l1_dssim_loss": (C.c_int, [_i32, _i32, _p, _p, _f, _f, _p, _p, _p, _p]),

@@ -38,8 +38,25 @@ int check_launch(const char* what) {
 
 constexpr int kPreThreads = 128;
 
+// Activations of the training parameters (the trainers' getters,
+// scripts/train_scanner_fixed.py:523-535): opacity = sigmoid(logit), scale =
+// exp(log_scale), rotation = q / (|q| + 1e-8). The training variants of the
+// preprocess forward and backward kernels both evaluate them from the flat
+// raw-parameter buffer with these functions (same file, same rounding), so no
+// activated copy is written or read.
+__device__ __forceinline__ float act_opacity(float logit) { return 1.0f / (1.0f + expf(-logit)); }
+__device__ __forceinline__ float act_scale(float log_scale) { return expf(log_scale); }
+__device__ __forceinline__ float4 raw_quat(const float* q4) {
+  return make_float4(q4[0], q4[1], q4[2], q4[3]);  // scalar loads: the segment may be unaligned
+}
+__device__ __forceinline__ float4 act_quat(float4 q) {
+  const float inv = 1.0f / (sqrtf(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w) + 1e-8f);
+  return make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
+}
+
 struct PreArgs {
   fgs_preprocess_params p;
+  const float* raw;  // training variant: the flat raw parameters (59 n floats)
   float focal_x, focal_y;
   int gx, gy;
   const float *means3d, *dc, *sh, *colors_precomp, *opacities, *scales, *quats, *cov3d_precomp,
@@ -125,6 +142,7 @@ __device__ __forceinline__ v3 sh_color(int deg, v3 dir_unnorm, const float* dcp,
   return out;
 }
 
+template <bool kRaw>
 __global__ void __launch_bounds__(kPreThreads) preprocess_fwd_kernel(PreArgs a) {
   extern __shared__ float s_sh[];
   const fgs_preprocess_params& p = a.p;
@@ -166,10 +184,12 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_fwd_kernel(PreArgs a) 
       // compute_cov3d, fastgs_preprocess.metal:207-231
       const float mod = p.scale_modifier;
       m3 s = M3(1.f, 0.f, 0.f, 0.f, 1.f, 0.f, 0.f, 0.f, 1.f);
-      s.c[0].x = mod * a.scales[3 * i];
-      s.c[1].y = mod * a.scales[3 * i + 1];
-      s.c[2].z = mod * a.scales[3 * i + 2];
-      const float4 q = reinterpret_cast<const float4*>(a.quats)[i];
+      const int64_t n = p.n;
+      s.c[0].x = mod * (kRaw ? act_scale(a.raw[52 * n + 3 * i]) : a.scales[3 * i]);
+      s.c[1].y = mod * (kRaw ? act_scale(a.raw[52 * n + 3 * i + 1]) : a.scales[3 * i + 1]);
+      s.c[2].z = mod * (kRaw ? act_scale(a.raw[52 * n + 3 * i + 2]) : a.scales[3 * i + 2]);
+      const float4 q = kRaw ? act_quat(raw_quat(a.raw + 55 * n + 4 * (int64_t)i))
+                            : reinterpret_cast<const float4*>(a.quats)[i];
       const float r = q.x, x = q.y, y = q.z, z = q.w;
       const m3 rm = M3(1.f - 2.f * (y * y + z * z), 2.f * (x * y - r * z), 2.f * (x * z + r * y),
                        2.f * (x * y + r * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z - r * x),
@@ -202,7 +222,8 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_fwd_kernel(PreArgs a) 
     const float det = cx * cz - cy * cy;
     if (det != 0.0f) {
       const float det_inv = 1.f / det;
-      const float4 co = make_float4(cz * det_inv, -cy * det_inv, cx * det_inv, a.opacities[i]);
+      const float op = kRaw ? act_opacity(a.raw[51 * (int64_t)p.n + i]) : a.opacities[i];
+      const float4 co = make_float4(cz * det_inv, -cy * det_inv, cx * det_inv, op);
       const float mid = 0.5f * (cx + cz);
       const float l1 = mid + sqrtf(fmax_t(0.1f, mid * mid - det));
       const float l2 = mid - sqrtf(fmax_t(0.1f, mid * mid - det));
@@ -369,7 +390,7 @@ struct PbwdArgs {
   float *dmeans3d, *ddc, *dsh, *dcolors_precomp, *dopac, *dscales, *dquats, *dvs_in;
   // training mode (kTrain): gradients w.r.t. the raw parameters, accumulated
   // into a flat buffer, plus densification statistics
-  const float *opac_act, *quats_raw;
+  const float* raw;  // the flat raw parameters (59 n floats)
   float *g_means, *g_dc, *g_rest, *g_logit, *g_logscale, *g_rot;
   float *st_acc, *st_acc_abs, *st_denom, *st_max_radii;
   int accumulate;
@@ -679,8 +700,16 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
         }
       }
       if (!P.use_cov3d_precomp) {
-        const v3 scale = V3(a.scales[3 * i], a.scales[3 * i + 1], a.scales[3 * i + 2]);
-        const float4 q = reinterpret_cast<const float4*>(a.quats)[i];
+        v3 scale;
+        float4 q;
+        if constexpr (kTrain) {
+          const float* ls = a.raw + 52 * (int64_t)P.n + 3 * (int64_t)i;
+          scale = V3(act_scale(ls[0]), act_scale(ls[1]), act_scale(ls[2]));
+          q = act_quat(raw_quat(a.raw + 55 * (int64_t)P.n + 4 * (int64_t)i));
+        } else {
+          scale = V3(a.scales[3 * i], a.scales[3 * i + 1], a.scales[3 * i + 2]);
+          q = reinterpret_cast<const float4*>(a.quats)[i];
+        }
         const float r = q.x, x = q.y, y = q.z, z = q.w;
         const m3 R = M3(1.f - 2.f * (y * y + z * z), 2.f * (x * y - r * z), 2.f * (x * z + r * y),
                         2.f * (x * y + r * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z - r * x),
@@ -736,15 +765,15 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
       // activation backward: opacity = sigmoid(logit), scale = exp(log_scale),
       // quat = q / (|q| + 1e-8) (the trainers' getters,
       // scripts/train_scanner_fixed.py:523-535)
-      const float o = a.opac_act[i];
+      const float o = act_opacity(a.raw[51 * (int64_t)P.n + i]);
       const float dlogit = dop * o * (1.0f - o);
       float dls[3];
 #pragma unroll
-      for (int c = 0; c < 3; ++c) dls[c] = dsc[c] * a.scales[3 * (int64_t)i + c];
+      for (int c = 0; c < 3; ++c)
+        dls[c] = dsc[c] * act_scale(a.raw[52 * (int64_t)P.n + 3 * (int64_t)i + c]);
       // scalar accesses to the flat buffers: their rotation segment starts at
       // 55 n floats, 16-byte aligned only when n is a multiple of 4
-      const float4 qr = make_float4(a.quats_raw[4 * (int64_t)i], a.quats_raw[4 * (int64_t)i + 1],
-                                    a.quats_raw[4 * (int64_t)i + 2], a.quats_raw[4 * (int64_t)i + 3]);
+      const float4 qr = raw_quat(a.raw + 55 * (int64_t)P.n + 4 * (int64_t)i);
       const float qn = sqrtf(qr.x * qr.x + qr.y * qr.y + qr.z * qr.z + qr.w * qr.w);
       const float inv = 1.0f / (qn + 1e-8f);
       const float qdot = qr.x * dq[0] + qr.y * dq[1] + qr.z * dq[2] + qr.w * dq[3];
@@ -865,6 +894,7 @@ int fgs_preprocess_forward(const fgs_preprocess_params* p, const float* means3d,
                 "xys and cov3d must be 8-byte, conic_opacity, viewspace_out and rotations "
                 "16-byte aligned");
   PreArgs a;
+  memset(&a, 0, sizeof(a));
   a.p = *p;
   a.focal_x = (float)p->image_width / (2.0f * p->tan_fovx);
   a.focal_y = (float)p->image_height / (2.0f * p->tan_fovy);
@@ -878,10 +908,51 @@ int fgs_preprocess_forward(const fgs_preprocess_params* p, const float* means3d,
   const bool use_sh = !p->use_colors_precomp && p->degree > 0 && p->max_sh_coeffs > 0;
   const size_t smem = use_sh ? (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
   static unsigned long long attr_done = 0;
-  if (smem > 48 * 1024) smem_attr_once(preprocess_fwd_kernel, (int)smem, &attr_done);
+  if (smem > 48 * 1024) smem_attr_once(preprocess_fwd_kernel<false>, (int)smem, &attr_done);
   const int blocks = (p->n + kPreThreads - 1) / kPreThreads;
-  preprocess_fwd_kernel<<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  preprocess_fwd_kernel<false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_forward");
+}
+
+int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const float* params,
+                                 const float* viewmatrix, const float* projmatrix,
+                                 const float* cam_pos, const float* viewspace_in, int32_t* radii,
+                                 float* xys, float* depths, float* cov3d, float* rgb,
+                                 float* conic_opacity, uint32_t* tiles_touched, uint8_t* clamped,
+                                 float* viewspace_out, void* stream) {
+  int st = validate_pre(p);
+  if (st) return st;
+  if (p->n == 0) return FGS_OK;
+  FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
+                "training mode needs the scales+quats and dc+sh paths");
+  FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
+  FGS_CHECK_ARG(params && viewmatrix && projmatrix && cam_pos && viewspace_in, "missing input pointer");
+  FGS_CHECK_ARG(radii && xys && depths && cov3d && rgb && conic_opacity && tiles_touched &&
+                    clamped && viewspace_out,
+                "missing output pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(xys, 8) && FGS_ALIGNED(cov3d, 8) && FGS_ALIGNED(conic_opacity, 16) &&
+                    FGS_ALIGNED(viewspace_out, 16),
+                "xys and cov3d must be 8-byte, conic_opacity and viewspace_out 16-byte aligned");
+  const int64_t n = p->n;
+  PreArgs a;
+  memset(&a, 0, sizeof(a));
+  a.p = *p;
+  a.focal_x = (float)p->image_width / (2.0f * p->tan_fovx);
+  a.focal_y = (float)p->image_height / (2.0f * p->tan_fovy);
+  a.gx = (p->image_width + 15) / 16;
+  a.gy = (p->image_height + 15) / 16;
+  a.raw = params;
+  a.means3d = params; a.dc = params + 3 * n; a.sh = params + 6 * n;
+  a.viewmatrix = viewmatrix; a.projmatrix = projmatrix; a.cam_pos = cam_pos; a.vs_in = viewspace_in;
+  a.radii = radii; a.xys = xys; a.depths = depths; a.cov3d = cov3d; a.rgb = rgb;
+  a.conic = conic_opacity; a.tiles = tiles_touched; a.clamped = clamped; a.vs_out = viewspace_out;
+  const bool use_sh = p->degree > 0;
+  const size_t smem = use_sh ? (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(preprocess_fwd_kernel<true>, (int)smem, &attr_done);
+  const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
+  preprocess_fwd_kernel<true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  return check_launch("preprocess_forward_train");
 }
 
 size_t fgs_scan_scratch_bytes(int64_t n) {
@@ -953,39 +1024,35 @@ int fgs_preprocess_backward(const fgs_preprocess_params* p, const float* means3d
   return check_launch("preprocess_backward");
 }
 
-int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* means3d,
-                                  const float* scales, const float* quats, const float* quats_raw,
-                                  const float* opacities, const float* viewmatrix,
-                                  const float* projmatrix, const float* cam_pos, const float* sh,
-                                  const float* cov3d_fwd, const float* dL_drgb,
-                                  const float* dL_dxys, const float* dL_dconic_opacity,
-                                  const float* dL_dviewspace, const int32_t* radii,
-                                  const uint8_t* clamped, int32_t accumulate, float* grad_flat,
-                                  float* stats, void* stream) {
+int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* params,
+                                  const float* viewmatrix, const float* projmatrix,
+                                  const float* cam_pos, const float* cov3d_fwd,
+                                  const float* dL_drgb, const float* dL_dxys,
+                                  const float* dL_dconic_opacity, const float* dL_dviewspace,
+                                  const int32_t* radii, const uint8_t* clamped, int32_t accumulate,
+                                  float* grad_flat, float* stats, void* stream) {
   int st = validate_pre(p);
   if (st) return st;
   if (p->n == 0) return FGS_OK;
   FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
                 "training mode needs the scales+quats and dc+sh paths");
   FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
-  FGS_CHECK_ARG(means3d && scales && quats && quats_raw && opacities && viewmatrix && projmatrix &&
-                    cam_pos && sh && cov3d_fwd && dL_drgb && dL_dxys && dL_dconic_opacity &&
-                    dL_dviewspace && radii && clamped && grad_flat && stats,
+  FGS_CHECK_ARG(params && viewmatrix && projmatrix && cam_pos && cov3d_fwd && dL_drgb && dL_dxys &&
+                    dL_dconic_opacity && dL_dviewspace && radii && clamped && grad_flat && stats,
                 "missing pointer");
-  FGS_CHECK_ARG(FGS_ALIGNED(quats, 16) && FGS_ALIGNED(dL_dconic_opacity, 16) &&
-                    FGS_ALIGNED(dL_dviewspace, 16),
-                "rotations, conic and viewspace gradients must be 16-byte aligned");
+  FGS_CHECK_ARG(FGS_ALIGNED(dL_dconic_opacity, 16) && FGS_ALIGNED(dL_dviewspace, 16),
+                "conic and viewspace gradients must be 16-byte aligned");
   const int64_t n = p->n;
   PbwdArgs a;
   memset(&a, 0, sizeof(a));
   a.p = *p;
   a.focal_x = 0.5f * (float)p->image_width / (p->tan_fovx < 1e-6f ? 1e-6f : p->tan_fovx);
   a.focal_y = 0.5f * (float)p->image_height / (p->tan_fovy < 1e-6f ? 1e-6f : p->tan_fovy);
-  a.means3d = means3d; a.scales = scales; a.quats = quats; a.vm = viewmatrix; a.pm = projmatrix;
-  a.cam_pos = cam_pos; a.sh = sh; a.cov3d_fwd = cov3d_fwd;
+  a.raw = params;
+  a.means3d = params; a.sh = params + 6 * n; a.vm = viewmatrix; a.pm = projmatrix;
+  a.cam_pos = cam_pos; a.cov3d_fwd = cov3d_fwd;
   a.drgb = dL_drgb; a.dxys = dL_dxys; a.dconic = dL_dconic_opacity; a.dvs_out = dL_dviewspace;
   a.radii = radii; a.clamped = clamped;
-  a.opac_act = opacities; a.quats_raw = quats_raw;
   a.g_means = grad_flat;
   a.g_dc = grad_flat + 3 * n;
   a.g_rest = grad_flat + 6 * n;
@@ -1005,29 +1072,26 @@ int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* m
   return check_launch("preprocess_backward_train");
 }
 
-int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* scales,
-                                 const float* quats, const float* opacities,
-                                 const float* viewmatrix, const float* projmatrix,
-                                 const float* cam_pos, const float* cov3d_fwd, const float* dL_drgb,
-                                 const float* dL_dxys, const float* dL_dconic_opacity,
-                                 const float* dL_dviewspace, const int32_t* radii,
-                                 const uint8_t* clamped, float* params, float* exp_avg,
-                                 float* exp_avg_sq, const float* group_lr, float beta1, float beta2,
-                                 float eps, int32_t step, int32_t bias_correction, float* stats,
-                                 void* stream) {
+int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* viewmatrix,
+                                 const float* projmatrix, const float* cam_pos,
+                                 const float* cov3d_fwd, const float* dL_drgb, const float* dL_dxys,
+                                 const float* dL_dconic_opacity, const float* dL_dviewspace,
+                                 const int32_t* radii, const uint8_t* clamped, float* params,
+                                 float* exp_avg, float* exp_avg_sq, const float* group_lr,
+                                 float beta1, float beta2, float eps, int32_t step,
+                                 int32_t bias_correction, float* stats, void* stream) {
   int st = validate_pre(p);
   if (st) return st;
   if (p->n == 0) return FGS_OK;
   FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
                 "training mode needs the scales+quats and dc+sh paths");
   FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
-  FGS_CHECK_ARG(scales && quats && opacities && viewmatrix && projmatrix && cam_pos && cov3d_fwd &&
-                    dL_drgb && dL_dxys && dL_dconic_opacity && dL_dviewspace && radii && clamped &&
-                    params && exp_avg && exp_avg_sq && group_lr && stats,
+  FGS_CHECK_ARG(viewmatrix && projmatrix && cam_pos && cov3d_fwd && dL_drgb && dL_dxys &&
+                    dL_dconic_opacity && dL_dviewspace && radii && clamped && params && exp_avg &&
+                    exp_avg_sq && group_lr && stats,
                 "missing pointer");
-  FGS_CHECK_ARG(FGS_ALIGNED(quats, 16) && FGS_ALIGNED(dL_dconic_opacity, 16) &&
-                    FGS_ALIGNED(dL_dviewspace, 16),
-                "rotations, conic and viewspace gradients must be 16-byte aligned");
+  FGS_CHECK_ARG(FGS_ALIGNED(dL_dconic_opacity, 16) && FGS_ALIGNED(dL_dviewspace, 16),
+                "conic and viewspace gradients must be 16-byte aligned");
   FGS_CHECK_ARG(!bias_correction || step >= 1, "step must be >= 1 with bias correction");
   const int64_t n = p->n;
   PbwdArgs a;
@@ -1035,15 +1099,14 @@ int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* sc
   a.p = *p;
   a.focal_x = 0.5f * (float)p->image_width / (p->tan_fovx < 1e-6f ? 1e-6f : p->tan_fovx);
   a.focal_y = 0.5f * (float)p->image_height / (p->tan_fovy < 1e-6f ? 1e-6f : p->tan_fovy);
-  // the raw means, sh rest and rotations are read from the parameter buffer
-  // that this launch updates: each Gaussian's values are read before its own
-  // update, and the sh rows are staged in shared memory first
-  a.means3d = params; a.sh = params + 6 * n; a.quats_raw = params + 55 * n;
-  a.scales = scales; a.quats = quats; a.vm = viewmatrix; a.pm = projmatrix;
+  // the raw parameters are read from the buffer that this launch updates: each
+  // Gaussian's values are read before its own update, and the sh rows are
+  // staged in shared memory first
+  a.raw = params;
+  a.means3d = params; a.sh = params + 6 * n; a.vm = viewmatrix; a.pm = projmatrix;
   a.cam_pos = cam_pos; a.cov3d_fwd = cov3d_fwd;
   a.drgb = dL_drgb; a.dxys = dL_dxys; a.dconic = dL_dconic_opacity; a.dvs_out = dL_dviewspace;
   a.radii = radii; a.clamped = clamped;
-  a.opac_act = opacities;
   a.st_acc = stats;
   a.st_acc_abs = stats + n;
   a.st_denom = stats + 2 * n;

@@ -321,9 +321,6 @@ class Trainer:
         self.last_cam = cm  # [view 16 | projection 16 | position 3] of this view
         prm = PreprocessParams(n, self.sh_degree, 15, 1.0, 1.0, float(cam.tan_fovx), float(cam.tan_fovy),
                                W, H, 0, 0)
-        means = self.view("means3d")
-        dc = self.view("features_dc")
-        rest = self.view("features_rest")
         vs_in = ws.get("vs_in", 4 * n, torch.float32)
         if not getattr(self, "_vs_zeroed", False) or vs_in.data_ptr() != getattr(self, "_vs_ptr", 0):
             vs_in.zero_()
@@ -337,9 +334,10 @@ class Trainer:
         tiles = ws.get("tiles", n, torch.uint32)
         clamped = ws.get("clamped", 3 * n, torch.uint8)
         vs_out = ws.get("vs_out", 4 * n, torch.float32)
-        self._call("preprocess", L.fgs_preprocess_forward, C.byref(prm), _p(means), _p(dc), _p(rest), None, _p(self.opacities), _p(self.scales),
-            _p(self.quats), None, _p(vm), _p(pm), _p(cp), _p(vs_in), _p(radii), _p(xys), _p(depths),
-            _p(cov3d), _p(rgb), _p(conic), _p(tiles), _p(clamped), _p(vs_out), st)
+        # activations (sigmoid, exp, normalise) are applied inside the kernels
+        self._call("preprocess", L.fgs_preprocess_forward_train, C.byref(prm), _p(self.params), _p(vm),
+                   _p(pm), _p(cp), _p(vs_in), _p(radii), _p(xys), _p(depths), _p(cov3d), _p(rgb),
+                   _p(conic), _p(tiles), _p(clamped), _p(vs_out), st)
         cap = self._key_cap
         kb = sort_key_bits(T)
         # depth-first binning: order the Gaussians by depth, emit keys in that
@@ -468,16 +466,16 @@ class Trainer:
             lr = self.lrs
             lrs = (C.c_float * 6)(lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations)
             self._call("preprocess_backward_adam", L.fgs_preprocess_backward_adam, C.byref(prm),
-                       _p(self.scales), _p(self.quats), _p(self.opacities), _p(vm), _p(pm), _p(cp),
+                       _p(vm), _p(pm), _p(cp),
                        _p(cov3d), _p(dcolors), _p(dmeans2d), _p(dconic), _p(dvs), _p(radii),
                        _p(clamped), _p(self.params), _p(self.exp_avg), _p(self.exp_avg_sq), lrs,
                        float(self.betas[0]), float(self.betas[1]), self.eps, self.step_count,
                        int(self.bias_correction), _p(self.step_stats if stats is None else stats), st)
             return img
-        self._call("preprocess_backward_train", L.fgs_preprocess_backward_train, C.byref(prm), _p(means), _p(self.scales), _p(self.quats), _p(self.view("rotations")),
-            _p(self.opacities), _p(vm), _p(pm), _p(cp), _p(rest), _p(cov3d), _p(dcolors),
-            _p(dmeans2d), _p(dconic), _p(dvs), _p(radii), _p(clamped), int(bool(accumulate)),
-            _p(self.grads), _p(self.step_stats), st)
+        self._call("preprocess_backward_train", L.fgs_preprocess_backward_train, C.byref(prm),
+                   _p(self.params), _p(vm), _p(pm), _p(cp), _p(cov3d), _p(dcolors), _p(dmeans2d),
+                   _p(dconic), _p(dvs), _p(radii), _p(clamped), int(bool(accumulate)),
+                   _p(self.grads), _p(self.step_stats), st)
         return img
 
     def global_stats(self) -> torch.Tensor:
@@ -490,6 +488,9 @@ class Trainer:
 
     # -- full step --------------------------------------------------------
     def activate(self):
+        """Activated copies of the parameters (self.opacities, self.scales,
+        self.quats) for callers that want them; the step's own kernels apply
+        the activations to the raw parameters themselves."""
         self._call("activate", lib().fgs_activate_params, self.n, _p(self.params), _p(self.opacities),
                    _p(self.scales), _p(self.quats), self._stream())
 
@@ -500,7 +501,6 @@ class Trainer:
         the local views (sum) lands in loss_out[0] (device)."""
         world, rank = self.world, self.rank
         mine = local_views(len(cams), world, rank)
-        self.activate()
         scale = 1.0 / max(len(cams), 1)  # mean loss over the whole batch
         if self.fuse_adam and world == 1 and len(mine) == 1:
             # the gradient is this one view's: Adam runs inside its backward

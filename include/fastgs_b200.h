@@ -305,38 +305,47 @@ FGS_API int fgs_preprocess_backward(const fgs_preprocess_params* p, const float*
 FGS_API int fgs_activate_params(int64_t n, const float* params_flat, float* opacities,
                                 float* scales, float* quats, void* stream);
 
-/* Preprocess backward for training: as fgs_preprocess_backward (scales+quats
- * and dc+sh paths, 15 SH rest coefficients), chained through the activations
- * above, written (accumulate == 0) or added (accumulate != 0) into the flat
- * gradient buffer, and the densification statistics of
- * scripts/train_scanner_fastgs.py:391-405 updated for Gaussians with
- * radii > 0 from dL_dviewspace. */
-FGS_API int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* means3d,
-                                          const float* scales, const float* quats,
-                                          const float* quats_raw, const float* opacities,
+/* Training variants of preprocess forward and backward. They read the flat
+ * raw-parameter buffer `params` (59 n floats: means 3, dc 3, sh rest 45,
+ * opacity logit 1, log-scale 3, rotation 4, each segment attribute-major) and
+ * apply the trainers' activations inside the kernels (opacity =
+ * sigmoid(logit), scale = exp(log_scale), rotation = q / (|q| + 1e-8):
+ * scripts/train_scanner_fixed.py:523-535), so no activated copy is needed.
+ * SH degree 3 layout (15 rest coefficients), scales+quats and dc+sh paths.
+ *
+ * fgs_preprocess_forward_train: the outputs of fgs_preprocess_forward.
+ *
+ * fgs_preprocess_backward_train: as fgs_preprocess_backward, chained through
+ * the activations, written (accumulate == 0) or added (accumulate != 0) into
+ * the flat gradient buffer, and the densification statistics of
+ * scripts/train_scanner_fastgs.py:391-405 ([acc | acc_abs | denom |
+ * max_radii], 4 n) updated for Gaussians with radii > 0 from dL_dviewspace.
+ *
+ * fgs_preprocess_backward_adam: the same backward pass of one view followed
+ * by the Adam step of fgs_adam_step, in one pass: each Gaussian's gradients
+ * are applied to params / exp_avg / exp_avg_sq as soon as they are formed, so
+ * no gradient buffer is written or read. group_lr[6] holds the learning rate
+ * of each segment in layout order. For a step whose gradient is exactly this
+ * one view's (one view, one rank); the result equals
+ * fgs_preprocess_backward_train + fgs_adam_step bit for bit. */
+FGS_API int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const float* params,
+                                         const float* viewmatrix, const float* projmatrix,
+                                         const float* cam_pos, const float* viewspace_in,
+                                         int32_t* radii, float* xys, float* depths, float* cov3d,
+                                         float* rgb, float* conic_opacity, uint32_t* tiles_touched,
+                                         uint8_t* clamped, float* viewspace_out, void* stream);
+FGS_API int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* params,
                                           const float* viewmatrix, const float* projmatrix,
-                                          const float* cam_pos, const float* sh,
-                                          const float* cov3d_fwd, const float* dL_drgb,
-                                          const float* dL_dxys, const float* dL_dconic_opacity,
+                                          const float* cam_pos, const float* cov3d_fwd,
+                                          const float* dL_drgb, const float* dL_dxys,
+                                          const float* dL_dconic_opacity,
                                           const float* dL_dviewspace, const int32_t* radii,
                                           const uint8_t* clamped, int32_t accumulate,
                                           float* grad_flat, float* stats, void* stream);
-
-/* fgs_preprocess_backward_train of one view followed by the Adam step of
- * fgs_adam_step, in one pass: each Gaussian's raw-parameter gradients are
- * applied to params / exp_avg / exp_avg_sq (flat layout, 59 n floats: means
- * 3, dc 3, sh rest 45, opacity logit 1, log-scale 3, rotation 4, each segment
- * attribute-major) as soon as they are formed, so no gradient buffer is
- * written or read. group_lr[6] holds the learning rate of each segment in that
- * order. The raw means, sh rest and rotations are read from params. For a
- * step whose gradient is exactly this one view's (one view, one rank); the
- * result equals fgs_preprocess_backward_train + fgs_adam_step bit for bit. */
-FGS_API int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* scales,
-                                         const float* quats, const float* opacities,
-                                         const float* viewmatrix, const float* projmatrix,
-                                         const float* cam_pos, const float* cov3d_fwd,
-                                         const float* dL_drgb, const float* dL_dxys,
-                                         const float* dL_dconic_opacity,
+FGS_API int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* viewmatrix,
+                                         const float* projmatrix, const float* cam_pos,
+                                         const float* cov3d_fwd, const float* dL_drgb,
+                                         const float* dL_dxys, const float* dL_dconic_opacity,
                                          const float* dL_dviewspace, const int32_t* radii,
                                          const uint8_t* clamped, float* params, float* exp_avg,
                                          float* exp_avg_sq, const float* group_lr, float beta1,

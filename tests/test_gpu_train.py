@@ -220,20 +220,17 @@ def test_adam_fused_into_backward_matches_separate(cuda_dev):
     V1, V2 = tr.exp_avg_sq[:total].clone(), tr.exp_avg_sq[:total].clone()
     G = torch.empty(total, device=cuda_dev)
     st1, st2 = torch.zeros(4 * n, device=cuda_dev), torch.zeros(4 * n, device=cuda_dev)
-    common = [p(tr.scales), p(tr.quats)]
     L = lib()
+    cams = [p(cm[0:16]), p(cm[16:32]), p(cm[32:35])]
     assert L.fgs_preprocess_backward_train(
-        C.byref(prm), p(P1), *common, p(P1[55 * n:]), p(tr.opacities), p(cm[0:16]), p(cm[16:32]),
-        p(cm[32:35]), p(P1[6 * n:]), p(ws["cov3d"]), p(gc), p(gm), p(gk), p(gv), p(ws["radii"]), p(ws["clamped"]), 0, p(G), p(st1),
-        None) == 0
+        C.byref(prm), p(P1), *cams, p(ws["cov3d"]), p(gc), p(gm), p(gk), p(gv), p(ws["radii"]),
+        p(ws["clamped"]), 0, p(G), p(st1), None) == 0
     ends = (C.c_int64 * 6)(*[k * n for k in (3, 6, 51, 52, 55, 59)])
     assert L.fgs_adam_step(total, p(P1), p(G), p(M1), p(V1), 6, ends, lrs, 0.9, 0.99, 1e-8, 2, 1,
                            None) == 0
     assert L.fgs_preprocess_backward_adam(
-        C.byref(prm), *common, p(tr.opacities), p(cm[0:16]), p(cm[16:32]), p(cm[32:35]),
-        p(ws["cov3d"]), p(gc), p(gm), p(gk), p(gv),
-        p(ws["radii"]), p(ws["clamped"]), p(P2), p(M2), p(V2), lrs, 0.9, 0.99, 1e-8, 2, 1, p(st2),
-        None) == 0
+        C.byref(prm), *cams, p(ws["cov3d"]), p(gc), p(gm), p(gk), p(gv), p(ws["radii"]),
+        p(ws["clamped"]), p(P2), p(M2), p(V2), lrs, 0.9, 0.99, 1e-8, 2, 1, p(st2), None) == 0
     torch.cuda.synchronize()
     assert not torch.equal(P1, tr.params)
     assert torch.equal(P1, P2)
