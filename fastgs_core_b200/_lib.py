@@ -46,6 +46,7 @@ _SIGS = {
     "fgs_sort_pairs_static": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p]),
     "fgs_tile_prep": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _p]),
     "fgs_tile_order": (C.c_int, [_i32, _p, _p, _p]),
+    "fgs_tile_prep_ordered": (C.c_int, [_i64, _i32] + [_p] * 7 + [_i64, _p]),
     "fgs_sort_pairs_bits": (C.c_int, [_i64, _i32, _i32] + [_p] * 5 + [_sz, _p]),
     "fgs_depth_order_workspace_bytes": (_sz, [_i32]),
     "fgs_depth_order": (C.c_int, [_i32] + [_p] * 5 + [_sz, _p]),

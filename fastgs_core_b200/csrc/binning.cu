@@ -306,8 +306,9 @@ __device__ __forceinline__ int tile_order_class(const uint32_t* ranges, int t) {
   return (int)min((ns + 15u) / 16u, (uint32_t)(kOrderClasses - 1));
 }
 
-__global__ void __launch_bounds__(1024)
-    tile_order_kernel(const uint32_t* __restrict__ ranges, int num_tiles, uint32_t* __restrict__ order) {
+// The counting sort of tile_order_kernel by one whole CTA (all threads call it).
+__device__ __forceinline__ void tile_order_cta(const uint32_t* __restrict__ ranges, int num_tiles,
+                                               uint32_t* __restrict__ order) {
   __shared__ uint32_t s_hist[kOrderClasses];
   for (int c = threadIdx.x; c < kOrderClasses; c += blockDim.x) s_hist[c] = 0;
   __syncthreads();
@@ -341,11 +342,17 @@ __global__ void __launch_bounds__(1024)
     order[atomicAdd(&s_hist[tile_order_class(ranges, t)], 1u)] = (uint32_t)t;
 }
 
+__global__ void __launch_bounds__(1024)
+    tile_order_kernel(const uint32_t* __restrict__ ranges, int num_tiles, uint32_t* __restrict__ order) {
+  tile_order_cta(ranges, num_tiles, order);
+}
+
 // one CTA: bucket counts, their inclusive scan and the total
 __global__ void __launch_bounds__(1024)
     bucket_count_kernel(const uint32_t* __restrict__ ranges, int num_tiles,
                         uint32_t* __restrict__ bucket_count, uint32_t* __restrict__ bucket_offsets,
-                        uint64_t* __restrict__ bucket_sum) {
+                        uint64_t* __restrict__ bucket_sum, uint32_t* __restrict__ order,
+                        uint32_t* __restrict__ bucket_to_tile, int64_t bucket_to_tile_len) {
   __shared__ uint32_t s_w[32];
   __shared__ uint32_t s_carry;
   if (threadIdx.x == 0) s_carry = 0;
@@ -383,6 +390,13 @@ __global__ void __launch_bounds__(1024)
     __syncthreads();
   }
   if (threadIdx.x == 0) *bucket_sum = s_carry;
+  // optional: the heaviest-first tile order, and bucket-to-tile entries past
+  // the bucket total marked invalid (a caller that sizes the bucket arrays by
+  // a bound instead of the total)
+  if (order) tile_order_cta(ranges, num_tiles, order);
+  if (bucket_to_tile)
+    for (int64_t b = (int64_t)s_carry + threadIdx.x; b < bucket_to_tile_len; b += blockDim.x)
+      bucket_to_tile[b] = 0xffffffffu;
 }
 
 static inline int sort_passes(int key_bits) { return (key_bits + 7) / 8; }
@@ -558,8 +572,27 @@ int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorte
   if (num_rendered > 0)
     tile_ranges_kernel<<<(unsigned)((num_rendered + 255) / 256), 256, 0, s>>>(sorted_keys, num_rendered,
                                                                               num_tiles, ranges);
-  bucket_count_kernel<<<1, 1024, 0, s>>>(ranges, num_tiles, bucket_count, bucket_offsets, bucket_sum);
+  bucket_count_kernel<<<1, 1024, 0, s>>>(ranges, num_tiles, bucket_count, bucket_offsets, bucket_sum,
+                                         nullptr, nullptr, 0);
   return check_launch("tile_prep");
+}
+
+int fgs_tile_prep_ordered(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorted_keys,
+                          uint32_t* ranges, uint32_t* bucket_count, uint32_t* bucket_offsets,
+                          uint64_t* bucket_sum, uint32_t* tile_order, uint32_t* bucket_to_tile,
+                          int64_t bucket_to_tile_len, void* stream) {
+  FGS_CHECK_ARG(num_rendered >= 0 && num_tiles > 0 && bucket_to_tile_len >= 0, "bad sizes");
+  FGS_CHECK_ARG(ranges && bucket_count && bucket_offsets && bucket_sum && tile_order, "missing pointer");
+  FGS_CHECK_ARG(num_rendered == 0 || sorted_keys, "missing keys");
+  FGS_CHECK_ARG(bucket_to_tile_len == 0 || bucket_to_tile, "missing bucket_to_tile");
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaMemsetAsync(ranges, 0, (size_t)num_tiles * 2 * sizeof(uint32_t), s);
+  if (num_rendered > 0)
+    tile_ranges_kernel<<<(unsigned)((num_rendered + 255) / 256), 256, 0, s>>>(sorted_keys, num_rendered,
+                                                                              num_tiles, ranges);
+  bucket_count_kernel<<<1, 1024, 0, s>>>(ranges, num_tiles, bucket_count, bucket_offsets, bucket_sum,
+                                         tile_order, bucket_to_tile, bucket_to_tile_len);
+  return check_launch("tile_prep_ordered");
 }
 
 int fgs_tile_order(int32_t num_tiles, const uint32_t* ranges, uint32_t* tile_order, void* stream) {

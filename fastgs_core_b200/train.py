@@ -421,22 +421,21 @@ class Trainer:
         bcount = ws.get("bcount", T, torch.uint32)
         boffs = ws.get("boffs", T, torch.uint32)
         bsum = ws.get("bsum", 1, torch.uint64)
-        self._call("tile_prep", L.fgs_tile_prep, K, T, _p(skeys), _p(ranges), _p(bcount), _p(boffs), _p(bsum), st)
         # every tile has at most ceil(n_t/32) <= n_t/32 + 1 buckets: size the
-        # bucket arrays by that bound instead of reading the sum back
+        # bucket arrays by that bound instead of reading the sum back; entries
+        # past the real sum get an invalid tile id (the backward pass skips them)
         Bmax = (K + 31) // 32 + T
         self.last_buckets_bound = Bmax
         b2t = ws.get("b2t", Bmax, torch.uint32)
-        b2t_i = b2t.view(torch.int32)
-        b2t_i.fill_(-1)  # buckets past the real sum keep an invalid tile id: backward skips them
+        order = ws.get("tile_order", T, torch.uint32)
+        self._call("tile_prep", L.fgs_tile_prep_ordered, K, T, _p(skeys), _p(ranges), _p(bcount),
+                   _p(boffs), _p(bsum), _p(order), _p(b2t), Bmax, st)
         samp_t = ws.get("samp_t", Bmax * 256, torch.float32)
         samp_ar = ws.get("samp_ar", Bmax * 768, torch.float32)
         final_t = ws.get("final_t", P, torch.float32)
         ncontrib = ws.get("ncontrib", P, torch.uint32)
         maxc = ws.get("maxc", T, torch.uint32)
         pixc = ws.get("pixc", 3 * P, torch.float32)
-        order = ws.get("tile_order", T, torch.uint32)
-        self._call("tile_order", L.fgs_tile_order, T, _p(ranges), _p(order), st)
         cm_ptr = None
         if self.contrib_mask:
             cm_ptr = ws.get("contrib_mask", Bmax * 256, torch.uint32).data_ptr()

@@ -203,6 +203,15 @@ FGS_API int fgs_tile_prep(int64_t num_rendered, int32_t num_tiles, const uint64_
 FGS_API int fgs_tile_order(int32_t num_tiles, const uint32_t* ranges, uint32_t* tile_order,
                            void* stream);
 
+/* fgs_tile_prep, fgs_tile_order and the invalidation of bucket_to_tile
+ * entries [bucket total, bucket_to_tile_len) in two launches, for a caller
+ * that sizes the bucket arrays by a bound (the backward pass skips buckets
+ * whose tile entry is out of range). */
+FGS_API int fgs_tile_prep_ordered(int64_t num_rendered, int32_t num_tiles, const uint64_t* sorted_keys,
+                                  uint32_t* ranges, uint32_t* bucket_count, uint32_t* bucket_offsets,
+                                  uint64_t* bucket_sum, uint32_t* tile_order, uint32_t* bucket_to_tile,
+                                  int64_t bucket_to_tile_len, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Rasterize forward: one CTA per 16x16 tile, front-to-back alpha blending
  * with early termination, per-32-splat bucket samples for the backward pass.

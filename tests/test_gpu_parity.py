@@ -231,3 +231,44 @@ def test_rasterize_backward_recompute_path(case, cuda_dev):
                          ("d_conic_opacity", "dconic_opacity"), ("d_viewspace_points", "dviewspace_raster")):
         got = g[mine].cpu().numpy().reshape(b[theirs].shape)
         assert rel_err(got, b[theirs]) < GRAD_TOL, (mine, rel_err(got, b[theirs]))
+
+
+def test_tile_prep_ordered_matches_parts(cuda_dev):
+    """fgs_tile_prep_ordered = fgs_tile_prep + fgs_tile_order + invalidating
+    bucket_to_tile past the bucket total."""
+    import ctypes as C
+
+    from fastgs_core_b200._lib import lib
+
+    rng = np.random.default_rng(11)
+    T = 1900
+    tiles = np.sort(rng.integers(0, T, 50_000)).astype(np.uint64)
+    keys = (tiles << np.uint64(32)) | rng.integers(0, 2**31, tiles.size).astype(np.uint64)
+    k = torch.from_numpy(keys.view(np.int64)).to(cuda_dev)
+    K = keys.size
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    outs = []
+    for ordered in (False, True):
+        ranges = torch.empty(2 * T, dtype=torch.int32, device=cuda_dev)
+        bc = torch.empty(T, dtype=torch.int32, device=cuda_dev)
+        bo = torch.empty(T, dtype=torch.int32, device=cuda_dev)
+        bs = torch.empty(1, dtype=torch.int64, device=cuda_dev)
+        order = torch.empty(T, dtype=torch.int32, device=cuda_dev)
+        blen = K // 32 + T
+        b2t = torch.full((blen,), 7, dtype=torch.int32, device=cuda_dev)
+        if ordered:
+            assert lib().fgs_tile_prep_ordered(K, T, p(k), p(ranges), p(bc), p(bo), p(bs), p(order),
+                                               p(b2t), blen, None) == 0
+        else:
+            assert lib().fgs_tile_prep(K, T, p(k), p(ranges), p(bc), p(bo), p(bs), None) == 0
+            assert lib().fgs_tile_order(T, p(ranges), p(order), None) == 0
+        torch.cuda.synchronize()
+        outs.append((ranges.cpu().numpy(), bc.cpu().numpy(), bo.cpu().numpy(), int(bs.item()),
+                     order.cpu().numpy(), b2t.cpu().numpy()))
+    (r1, c1, o1, s1, ord1, _), (r2, c2, o2, s2, ord2, b2t) = outs
+    assert np.array_equal(r1, r2) and np.array_equal(c1, c2) and np.array_equal(o1, o2) and s1 == s2
+    counts = r2[1::2].astype(np.int64) - r2[0::2]
+    assert np.array_equal(np.sort(ord2), np.arange(T))
+    cls = np.minimum((counts[ord2] + 15) // 16, 255)
+    assert np.all(np.diff(cls) <= 0)
+    assert np.all(b2t[:s2] == 7) and np.all(b2t[s2:] == -1)
