@@ -46,6 +46,11 @@ _SIGS = {
     "fgs_sort_pairs_static": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p]),
     "fgs_tile_prep": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _p]),
     "fgs_tile_order": (C.c_int, [_i32, _p, _p, _p]),
+    "fgs_gather_rows": (C.c_int, [_i64, _i64, _p, _i32, _p, _p, _p, _p]),
+    "fgs_densify_masks": (C.c_int, [_i64, _p, _p, _p, _f, _f, _f, _f, _p, _p]),
+    "fgs_prune_masks": (C.c_int, [_i64, _p, _p, _f, _f, _f, _p, _p]),
+    "fgs_split_fixup": (C.c_int, [_i64, _i64, _i64, _p, _i32, _p, _p]),
+    "fgs_opacity_cap": (C.c_int, [_i64, _f, _p, _p, _p, _p]),
     "fgs_tile_prep_ordered": (C.c_int, [_i64, _i32] + [_p] * 7 + [_i64, _p]),
     "fgs_sort_pairs_bits": (C.c_int, [_i64, _i32, _i32] + [_p] * 5 + [_sz, _p]),
     "fgs_depth_order_workspace_bytes": (_sz, [_i32]),

@@ -22,7 +22,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libfastgs_b200.so")
-SOURCES = ["preprocess.cu", "binning.cu", "raster.cu", "raster_bwd.cu", "train.cu"]
+SOURCES = ["preprocess.cu", "binning.cu", "raster.cu", "raster_bwd.cu", "train.cu", "densify.cu"]
 # files whose kernels may contract multiply-adds (their exact decisions use
 # explicitly rounded intrinsics)
 FMAD_OK = {"raster_bwd.cu", "train.cu"}

@@ -233,6 +233,32 @@ class Trainer:
         self.events: dict[str, list] = {}
         self.launches = 0
 
+    def _resize(self, n_new: int, params_new: torch.Tensor, exp_avg_new: torch.Tensor,
+                exp_avg_sq_new: torch.Tensor, stats_new: torch.Tensor) -> None:
+        """Adopt buffers for n_new Gaussians (densification): the flat
+        parameters and moments (padded to the layout's shard size), the
+        running statistics [acc | acc_abs | denom | max_radii]; gradients and
+        per-step statistics restart at zero."""
+        if self.world > 1:
+            raise NotImplementedError("densification runs on one rank (world size 1)")
+        d = self.dev
+        total = FLOATS_PER_GAUSSIAN * n_new
+        self.n = n_new
+        self._per = -(-total // 4) * 4
+        self.params_pad, self.exp_avg, self.exp_avg_sq = params_new, exp_avg_new, exp_avg_sq_new
+        assert params_new.numel() == self._per and exp_avg_new.numel() == self._per
+        self.grads_pad = torch.zeros(self._per, device=d)
+        self.params = self.params_pad[:total]
+        self.grads = self.grads_pad[:total]
+        self._lo, self._hi = 0, total
+        self.stats = stats_new
+        self.step_stats = torch.zeros((STATS_SUM + 1) * n_new, device=d)
+        self.opacities = torch.empty(n_new, device=d)
+        self.scales = torch.empty((n_new, 3), device=d)
+        self.quats = torch.empty((n_new, 4), device=d)
+        ends = np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n_new
+        self._group_end = (C.c_int64 * 6)(*ends.tolist())
+
     # kernels each C entry point launches (memsets are not kernels)
     _KERNELS = {"preprocess": 1, "depth_order": 8, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
                 "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1,

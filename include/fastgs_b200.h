@@ -417,6 +417,44 @@ FGS_API int fgs_score_finalize(int64_t n, const float* counts_acc, const float* 
                                int32_t n_views, float* importance, float* pruning, void* scratch,
                                void* stream);
 
+/* ---------------------------------------------------------------------------
+ * FastGS densification on the device (scripts/train_scanner_fastgs.py:470-795).
+ * Flat layouts as the training entry points: segment k of width w_k holds
+ * rows [0, n) attribute-major at offset (w_0 + ... + w_{k-1}) * n.
+ *
+ * fgs_gather_rows: dst row j of every segment = src row index[j] (n_in rows
+ * in src, n_out in dst; index < 0 writes zeros). Prunes (keep indices),
+ * appends copies (0..n-1 then the sources) and appends zero rows (moments).
+ *
+ * fgs_densify_masks: per Gaussian, bit 0 = clone (importance > threshold,
+ * max scale <= dense_extent, |acc / max(denom, 1)| >= grad_thresh), bit 1 =
+ * split (importance > threshold, max scale > dense_extent, |acc_abs /
+ * max(denom, 1)| >= grad_abs_thresh), bit 2 = importance > threshold.
+ * stats = [acc | acc_abs | denom | max_radii].
+ *
+ * fgs_prune_masks: bit 0 = sigmoid(logit) < min_opacity, bit 1 = max_radii >
+ * max_screen (max_screen > 0), bit 2 = max scale > max_world (max_world > 0).
+ *
+ * fgs_split_fixup: rows [row0, row0 + m) hold copies of their split sources;
+ * their means move by R(q) * samples[t] (samples already scaled by the
+ * source's scales) and their log-scales become log(exp(s) / (0.8 f)).
+ *
+ * fgs_opacity_cap: logit(clip(min(sigmoid(l), cap), 1e-6, 1 - 1e-6)) on the
+ * opacity segment; the opacity moments (if given) restart at zero. */
+FGS_API int fgs_gather_rows(int64_t n_in, int64_t n_out, const int64_t* index, int32_t num_segments,
+                            const int32_t* widths, const float* src, float* dst, void* stream);
+FGS_API int fgs_densify_masks(int64_t n, const float* params, const float* stats,
+                              const float* importance, float grad_thresh, float grad_abs_thresh,
+                              float dense_extent, float importance_thresh, uint8_t* mask,
+                              void* stream);
+FGS_API int fgs_prune_masks(int64_t n, const float* params, const float* max_radii,
+                            float min_opacity, float max_screen, float max_world, uint8_t* mask,
+                            void* stream);
+FGS_API int fgs_split_fixup(int64_t n, int64_t row0, int64_t m, const float* samples,
+                            int32_t split_factor, float* params, void* stream);
+FGS_API int fgs_opacity_cap(int64_t n, float cap, float* params, float* exp_avg, float* exp_avg_sq,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

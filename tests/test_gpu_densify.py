@@ -1,0 +1,147 @@
+"""GPU densification (fastgs_core_b200.densify) against the CPU restatement
+of the reference's FastGS densification (oracle/densify_ref.py), with the
+same seeded random generator on both sides. Row copies, moments and
+statistics compare bit for bit; the split children's means and scales and
+the capped opacity logits within 1e-5 relative (device exp/log)."""
+import numpy as np
+import pytest
+import torch
+
+from fastgs_core_b200 import densify as D
+from fastgs_core_b200 import synthetic as S
+from fastgs_core_b200.train import Trainer
+from oracle import densify_ref as R
+
+pytestmark = pytest.mark.gpu
+
+NAMES = R.PARAMS
+WIDTHS = dict(zip(NAMES, D.PARAM_WIDTHS))
+SHAPES = {"means3d": (3,), "features_dc": (3,), "features_rest": (15, 3), "opacity_logits": (),
+          "log_scales": (3,), "rotations": (4,)}
+
+
+def split_flat(flat, n):
+    out, off = {}, 0
+    for k in NAMES:
+        w = WIDTHS[k]
+        out[k] = flat[off * n:(off + w) * n].reshape((n,) + SHAPES[k])
+        off += w
+    return out
+
+
+def make_trainer(cuda_dev, n=3000, seed=0):
+    """A trainer with random parameters, moments and statistics, kept away
+    from every decision threshold (so device and host exp agree on them)."""
+    rng = np.random.default_rng(seed)
+    scene, _ = S.small_scene(seed, n, 3, 64, 64)
+    extent = 5.0
+    dense = 0.01 * extent
+    big = rng.random(n) < 0.5
+    scene.log_scales[:] = np.where(big[:, None], np.log(dense * rng.uniform(2, 4, (n, 3))),
+                                   np.log(dense * rng.uniform(0.1, 0.5, (n, 3)))).astype(np.float32)
+    low = rng.random(n) < 0.2
+    scene.opacity_logits[:] = np.where(low, rng.uniform(-9, -7, n), rng.uniform(-2, 3, n)).astype(np.float32)
+    tr = Trainer(scene, cuda_dev)
+    total = 59 * n
+    tr.exp_avg[:total] = torch.from_numpy(rng.normal(0, 1e-3, total).astype(np.float32)).to(cuda_dev)
+    tr.exp_avg_sq[:total] = torch.from_numpy(rng.uniform(0, 1e-6, total).astype(np.float32)).to(cuda_dev)
+    denom = rng.integers(0, 20, n).astype(np.float32)
+    acc = np.where(rng.random(n) < 0.5, 1e-3, 1e-5).astype(np.float32) * np.maximum(denom, 1)
+    acc_abs = np.where(rng.random(n) < 0.5, 5e-3, 1e-5).astype(np.float32) * np.maximum(denom, 1)
+    maxr = np.where(rng.random(n) < 0.1, 30.0, 5.0).astype(np.float32)
+    tr.stats.copy_(torch.from_numpy(np.concatenate([acc, acc_abs, denom, maxr])).to(cuda_dev))
+    importance = np.where(rng.random(n) < 0.6, 10.0, 1.0).astype(np.float32)
+    pruning = rng.uniform(0, 0.99, n).astype(np.float32)
+    return tr, extent, importance, pruning
+
+
+def oracle_state(tr, pruning=None):
+    n = tr.n
+    params = split_flat(tr.params.cpu().numpy(), n)
+    m = split_flat(tr.exp_avg[:59 * n].cpu().numpy(), n)
+    v = split_flat(tr.exp_avg_sq[:59 * n].cpu().numpy(), n)
+    st = tr.stats.cpu().numpy()
+    stats = {"xyz_grad_accum": st[:n], "xyz_grad_accum_abs": st[n:2 * n], "denom": st[2 * n:3 * n],
+             "max_radii2d": st[3 * n:], "tmp_radii": np.zeros(n, np.float32)}
+    return R.State(params, {k: (m[k], v[k]) for k in NAMES}, stats, pruning)
+
+
+def compare(tr, st, approx=()):
+    n = tr.n
+    assert n == st.n
+    got = split_flat(tr.params.cpu().numpy(), n)
+    gm = split_flat(tr.exp_avg[:59 * n].cpu().numpy(), n)
+    gv = split_flat(tr.exp_avg_sq[:59 * n].cpu().numpy(), n)
+    for k in NAMES:
+        if k in approx:
+            np.testing.assert_allclose(got[k], st.params[k], rtol=1e-5, atol=1e-6, err_msg=k)
+        else:
+            assert np.array_equal(got[k], st.params[k]), k
+        assert np.array_equal(gm[k], st.adam[k][0]), k
+        assert np.array_equal(gv[k], st.adam[k][1]), k
+    s = tr.stats.cpu().numpy()
+    for i, k in enumerate(("xyz_grad_accum", "xyz_grad_accum_abs", "denom", "max_radii2d")):
+        assert np.array_equal(s[i * n:(i + 1) * n], st.stats[k]), k
+
+
+def test_prune_points(cuda_dev):
+    tr, _, _, pruning = make_trainer(cuda_dev, 2001, 1)
+    st = oracle_state(tr, pruning)
+    mask = np.random.default_rng(5).random(tr.n) < 0.3
+    R.prune_points(st, mask)
+    score = D.prune_points(tr, mask, pruning)
+    compare(tr, st)
+    assert np.array_equal(score, st.score)
+
+
+def test_clone_and_split(cuda_dev):
+    tr, _, _, pruning = make_trainer(cuda_dev, 1500, 2)
+    st = oracle_state(tr, pruning)
+    g = np.random.default_rng(9)
+    metric = g.random(tr.n) < 0.5
+    clone = g.random(tr.n) < 0.3
+    split = ~clone & (g.random(tr.n) < 0.5)
+    c1, sc = D.densify_and_clone(tr, metric, clone, pruning)
+    c2 = R.densify_and_clone(st, metric, clone)
+    assert c1 == c2 > 0
+    r1, r2 = np.random.default_rng(77), np.random.default_rng(77)
+    a = D.densify_and_split(tr, metric, split, r1, 2, sc)
+    b = R.densify_and_split(st, metric, split, r2, 2)
+    assert a[:2] == b and a[0] > 0
+    compare(tr, st, approx=("means3d", "log_scales"))
+    assert np.array_equal(a[2], st.score)
+
+
+def test_densify_and_prune_fastgs(cuda_dev):
+    tr, extent, importance, pruning = make_trainer(cuda_dev, 4000, 3)
+    st = oracle_state(tr, pruning)
+    args = D.DensifyArgs()
+    got = D.densify_and_prune_fastgs(tr, args, extent, importance, pruning, np.random.default_rng(123))
+    want = R.densify_and_prune(st, args, extent, importance, np.random.default_rng(123))
+    assert got == want
+    assert got["cloned"] > 0 and got["split_sources"] > 0 and got["actual_removed"] > 0
+    compare(tr, st, approx=("means3d", "log_scales", "opacity_logits"))
+    # the trainer keeps training on the new set of Gaussians
+    _, cam = S.small_scene(3, 10, 3, 64, 64)
+    target = torch.rand(3 * 64 * 64, generator=torch.Generator().manual_seed(1)).to(cuda_dev)
+    lo = torch.zeros(4, device=cuda_dev)
+    tr.step([cam], [target], loss_out=lo)
+    torch.cuda.synchronize()
+    assert np.isfinite(lo[0].item())
+
+
+def test_final_prune_keeps_minimum(cuda_dev):
+    tr, _, _, pruning = make_trainer(cuda_dev, 500, 4)
+    st = oracle_state(tr)
+    got = D.final_prune_fastgs(tr, 0.5, pruning, 0.1, 300)
+    want = R.final_prune(st, 0.5, pruning, 0.1, 300)
+    assert got == want and got["kept"] == 300
+    compare(tr, st)
+
+
+def test_opacity_reset(cuda_dev):
+    tr, _, _, _ = make_trainer(cuda_dev, 700, 5)
+    st = oracle_state(tr)
+    D.reset_opacity_logits(tr, 0.05)
+    R.set_opacity_cap(st, 0.05)
+    compare(tr, st, approx=("opacity_logits",))
