@@ -213,6 +213,45 @@ def densify_and_prune_fastgs(tr, args: DensifyArgs, scene_extent: float, importa
             "actual_removed": removed}
 
 
+def compute_gaussian_scores_fastgs(tr, cams, targets, camera_indices, loss_thresh: float,
+                                   densify: bool):
+    """compute_gaussian_scores_fastgs (:268-340): for each sampled view, the
+    render, the min-max normalised per-pixel L1 map thresholded into a metric
+    map, a second render counting each Gaussian's metric pixels, and the
+    scores folded over the views (importance = floor(counts / views) when
+    densify, pruning = min-max normalised sum of photometric loss x counts).
+    targets[i] is the [3, H*W] float32 device target of cams[i]. Returns
+    (importance or None, pruning) as numpy arrays."""
+    L = lib()
+    n, dev = tr.n, tr.dev
+    st = torch.cuda.current_stream(dev).cuda_stream
+    counts = torch.zeros(n, device=dev)
+    score = torch.zeros(n, device=dev)
+    mcount = torch.empty(n, dtype=torch.int32, device=dev)
+    idx = [int(i) for i in np.asarray(camera_indices).reshape(-1)]
+    if not idx:
+        z = np.zeros(n, np.float32)
+        return (z if densify else None), z
+    for i in idx:
+        cam, target = cams[i], targets[i]
+        P = cam.width * cam.height
+        pred = tr.render_view(cam).clone()
+        mmap = torch.empty(P, dtype=torch.int32, device=dev)
+        l1 = torch.empty(1, device=dev)
+        scratch = torch.empty(P + 2, device=dev)
+        check(L.fgs_metric_map(P, _p(pred), _p(target), float(loss_thresh), _p(mmap), _p(l1),
+                               _p(scratch), st), "metric_map")
+        tr.render_view(cam, metric_map=mmap, metric_count=mcount)
+        check(L.fgs_score_accumulate(n, _p(mcount), _p(l1), 3 * P, _p(counts), _p(score), st),
+              "score_accumulate")
+    imp = torch.empty(n, device=dev)
+    pruning = torch.empty(n, device=dev)
+    fin = torch.empty(2, dtype=torch.int32, device=dev)
+    check(L.fgs_score_finalize(n, _p(counts), _p(score), len(idx), _p(imp) if densify else None,
+                               _p(pruning), _p(fin), st), "score_finalize")
+    return (imp.cpu().numpy() if densify else None), pruning.cpu().numpy()
+
+
 def final_prune_fastgs(tr, min_opacity: float, pruning_score, score_thresh: float,
                        min_gaussians: int) -> dict:
     """final_prune_fastgs (:748-795)."""

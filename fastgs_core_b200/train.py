@@ -315,7 +315,7 @@ class Trainer:
         return C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
 
     def render_view(self, cam, target=None, accumulate=False, loss_out=None, loss_scale=1.0,
-                    fused_adam=False, stats=None):
+                    fused_adam=False, stats=None, metric_map=None, metric_count=None):
         """Forward (and, with a target, loss + backward accumulated into the
         flat gradient buffer) of one view. Returns the image [3, H*W]. With
         fused_adam the backward pass applies the Adam step (of step number
@@ -465,10 +465,14 @@ class Trainer:
         cm_ptr = None
         if self.contrib_mask:
             cm_ptr = ws.get("contrib_mask", Bmax * 256, torch.uint32).data_ptr()
-        rp = RasterParams(W, H, T, Bmax, n, 0, order.data_ptr(), cm_ptr)
+        # FastGS metric counting (a second render of a sampled view,
+        # scripts/train_scanner_fastgs.py:313): metric_map [P] int32 in,
+        # metric_count [n] int32 out
+        get_flag = int(metric_map is not None)
+        rp = RasterParams(W, H, T, Bmax, n, get_flag, order.data_ptr(), cm_ptr)
         self._call("rasterize_forward", L.fgs_rasterize_forward, C.byref(rp), _p(ranges), _p(svals), _p(boffs), _p(xys), _p(rgb), _p(conic),
-            _p(self.background), None, _p(b2t), _p(samp_t), _p(samp_ar), _p(final_t), _p(ncontrib),
-            _p(maxc), _p(pixc), _p(img), None, st)
+            _p(self.background), _p(metric_map), _p(b2t), _p(samp_t), _p(samp_ar), _p(final_t), _p(ncontrib),
+            _p(maxc), _p(pixc), _p(img), _p(metric_count), st)
         if target is None:
             return img
         # loss and its gradient w.r.t. the image

@@ -145,3 +145,31 @@ def test_opacity_reset(cuda_dev):
     D.reset_opacity_logits(tr, 0.05)
     R.set_opacity_cap(st, 0.05)
     compare(tr, st, approx=("opacity_logits",))
+
+
+def test_scores_fold_views(cuda_dev):
+    """compute_gaussian_scores_fastgs: the metric map of each sampled view,
+    the counting render and the folding, against the same steps in torch."""
+    scene, cam = S.small_scene(6, 3000, 3, 96, 64, log_scale_mu=-3.0)
+    cams = [cam, S.look_at_camera((0.5, 0.3, 4.0), (0, 0, 0), 96, 64, 55.0)]
+    g = torch.Generator().manual_seed(8)
+    P = 96 * 64
+    targets = [torch.rand(3 * P, generator=g).to(cuda_dev) for _ in cams]
+    tr = Trainer(scene, cuda_dev)
+    imp, pr = D.compute_gaussian_scores_fastgs(tr, cams, targets, [1, 0], 0.06, True)
+    n = scene.n
+    counts = torch.zeros(n, device=cuda_dev)
+    score = torch.zeros(n, device=cuda_dev)
+    for i in (1, 0):
+        pred = tr.render_view(cams[i]).clone()
+        l1 = (pred.view(3, P) - targets[i].view(3, P)).abs()
+        lm = l1.mean(0)
+        mm = (((lm - lm.min()) / torch.clamp(lm.max() - lm.min(), min=1e-6)) > 0.06).int()
+        mc = torch.empty(n, dtype=torch.int32, device=cuda_dev)
+        tr.render_view(cams[i], metric_map=mm, metric_count=mc)
+        counts += mc.float()
+        score += l1.mean() * mc.float()
+    assert counts.sum().item() > 0
+    assert np.array_equal(imp, torch.floor(counts / 2).cpu().numpy())
+    s = score.cpu().numpy()
+    np.testing.assert_allclose(pr, (s - s.min()) / max(s.max() - s.min(), 1e-6), rtol=1e-4, atol=1e-5)
