@@ -110,6 +110,9 @@ __device__ __forceinline__ float power_cut(float o) { return o <= 1.0f ? -5.55f 
 // produces the same bits whatever its file's contraction setting.
 __device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g, float lr, float b1,
                                           float b2, float eps, float bc1, float bc2) {
+  // a negative learning rate marks a parameter group that does not step this
+  // iteration: its value and moments stay as they are
+  if (lr < 0.0f) return;
   m = __fmaf_rn(b1, m, __fmul_rn(1.0f - b1, g));
   v = __fmaf_rn(b2, v, __fmul_rn(__fmul_rn(1.0f - b2, g), g));
   p = __fsub_rn(p, __fdiv_rn(__fmul_rn(lr, __fmul_rn(m, bc1)),

@@ -417,6 +417,7 @@ __device__ __forceinline__ void adam_block(const PbwdArgs& a, int64_t seg, int w
   float* __restrict__ P = a.ap + seg + (int64_t)base * width;
   float* __restrict__ M = a.am + seg + (int64_t)base * width;
   float* __restrict__ V = a.av + seg + (int64_t)base * width;
+  if (lr < 0.0f) return;  // the group does not step this iteration
   const int count = cnt * width;
   for (int k0 = threadIdx.x; k0 < count; k0 += 4 * kPreThreads) {
     float pv[4], mv[4], vv[4];

@@ -336,7 +336,11 @@ FGS_API int fgs_activate_params(int64_t n, const float* params_flat, float* opac
  * no gradient buffer is written or read. group_lr[6] holds the learning rate
  * of each segment in layout order. For a step whose gradient is exactly this
  * one view's (one view, one rank); the result equals
- * fgs_preprocess_backward_train + fgs_adam_step bit for bit. */
+ * fgs_preprocess_backward_train + fgs_adam_step bit for bit.
+ *
+ * In every Adam entry point a negative group learning rate means that the
+ * group does not step: its values and moments are left unchanged (the
+ * reference's optimiser cadence, scripts/train_scanner_fastgs.py:160-183). */
 FGS_API int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const float* params,
                                          const float* viewmatrix, const float* projmatrix,
                                          const float* cam_pos, const float* viewspace_in,

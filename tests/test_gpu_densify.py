@@ -173,3 +173,39 @@ def test_scores_fold_views(cuda_dev):
     assert np.array_equal(imp, torch.floor(counts / 2).cpu().numpy())
     s = score.cpu().numpy()
     np.testing.assert_allclose(pr, (s - s.min()) / max(s.max() - s.min(), 1e-6), rtol=1e-4, atol=1e-5)
+
+
+def test_driver_schedule_runs(cuda_dev):
+    """FastGSDriver: the reference's loop schedule with densification, an
+    opacity reset and a final prune inside a short run; frozen groups do not
+    move."""
+    from fastgs_core_b200.policy import DriverConfig, FastGSDriver
+
+    scene, cam = S.small_scene(12, 4000, 3, 96, 64, log_scale_mu=-3.5)
+    cams = [cam] + [S.look_at_camera((0.4 * k, 0.2, 4.0), (0, 0, 0), 96, 64, 55.0) for k in range(1, 4)]
+    g = torch.Generator().manual_seed(4)
+    targets = [torch.rand(3 * 96 * 64, generator=g).to(cuda_dev) for _ in cams]
+    tr = Trainer(scene, cuda_dev)
+    cfg = DriverConfig(sh_degree_interval=5, stage_color_steps=3, densify_from_step=4,
+                       densify_until_step=30, densification_interval=8, opacity_reset_interval=20,
+                       densify_camera_sample=3, final_prune_start=30, final_prune_end=50,
+                       final_prune_interval=35, final_prune_min_gaussians=100)
+    cfg.densify.importance_score_threshold = 0.5
+    cfg.densify.grad_thresh = 1e-7
+    cfg.densify.grad_abs_thresh = 1e-7
+    drv = FastGSDriver(tr, cams, targets, cfg, seed=7)
+    n = tr.n
+    dc0 = tr.params[3 * n:6 * n].clone()
+    drv.step()
+    torch.cuda.synchronize()
+    assert torch.equal(tr.params[3 * n:6 * n], dc0)  # colours staged out for 3 steps
+    lo = torch.zeros(4, device=cuda_dev)
+    outs = [drv.step(loss_out=lo) for _ in range(39)]
+    torch.cuda.synchronize()
+    assert np.isfinite(lo[0].item())
+    dens = [o["densify"] for o in outs if "densify" in o]
+    assert dens and any(d["cloned"] + d["split_sources"] > 0 for d in dens)
+    assert any("opacity_reset" in o for o in outs)
+    assert any("final_prune" in o for o in outs)
+    assert drv.active_sh_degree == 3
+    assert tr.n != n
