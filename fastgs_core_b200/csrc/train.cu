@@ -289,13 +289,17 @@ struct AdamGroups {
   int count;
 };
 
+// learning rate of the group holding flat element idx (the last group past
+// every end); a fully unrolled search, so the table stays in registers
 __device__ __forceinline__ float adam_lr(const AdamGroups& grp, int64_t idx) {
-  float lr = grp.lr[grp.count - 1];
-  for (int q = 0; q < grp.count; ++q)
-    if (idx < grp.end[q]) {
-      lr = grp.lr[q];
-      break;
-    }
+  float lr = 0.0f;
+  bool found = false;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const bool hit = !found && q < grp.count && (idx < grp.end[q] || q == grp.count - 1);
+    lr = hit ? grp.lr[q] : lr;
+    found = found || hit;
+  }
   return lr;
 }
 
@@ -398,13 +402,7 @@ __device__ __forceinline__ void adam4(float4& pp, float4& mm, float4& vv, const 
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int64_t idx = idx0 + k;
-    float lr = grp.lr[grp.count - 1];
-    for (int q = 0; q < grp.count; ++q)
-      if (idx < grp.end[q]) {
-        lr = grp.lr[q];
-        break;
-      }
-    adam_elem(pa[k], ma[k], va[k], ga[k], lr, b1, b2, eps, bc1, bc2);
+    adam_elem(pa[k], ma[k], va[k], ga[k], adam_lr(grp, idx), b1, b2, eps, bc1, bc2);
   }
 }
 

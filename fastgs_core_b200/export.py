@@ -1,4 +1,4 @@
-"""Export of a trained set of Gaussians (SURVEY rank 3 of the "next" rows):
+"""Export of a trained set of Gaussians:
 
 * the arrays the reference hands to the spz library (save_as_spz,
   scripts/train_scanner_fixed.py:631-688): log-scales, opacity logits, dc
