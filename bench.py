@@ -326,6 +326,7 @@ def main():
 
     # ---------------- value: everything resident in HBM
     tr.record = {"rasterize_backward", "rasterize_forward", "adam", "loss", "reduce", "allgather", "exchange",
+                 "depth_order",
                  "preprocess_backward_train", "preprocess_backward_adam", "sort", "preprocess"}
     tr.events.clear()
     clocks = ClockSampler(local)
@@ -350,7 +351,8 @@ def main():
     launches = (tr.launches - launches0) // args.steps
     bwd_ms = tr.kernel_ms("rasterize_backward")
     fwd_ms = tr.kernel_ms("rasterize_forward")
-    stage_ms = {k: tr.kernel_ms(k) for k in ("preprocess", "sort", "loss", "preprocess_backward_train",
+    stage_ms = {k: tr.kernel_ms(k) for k in ("preprocess", "depth_order", "sort", "loss",
+                                              "preprocess_backward_train",
                                               "preprocess_backward_adam", "adam", "reduce", "allgather",
                                               "exchange")}
     tr.record = set()
