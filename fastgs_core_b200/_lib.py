@@ -44,6 +44,8 @@ _SIGS = {
     "fgs_sort_workspace_bytes": (_sz, [_i64, _i32]),
     "fgs_sort_pairs": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _sz, _p]),
     "fgs_sort_pairs_static": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p]),
+    "fgs_sort_status": (C.c_int, [_p, _p]),
+    "fgs_sort_set_test_hooks": (C.c_int, [_i32, _i32]),
     "fgs_tile_prep": (C.c_int, [_i64, _i32, _p, _p, _p, _p, _p, _p]),
     "fgs_tile_order": (C.c_int, [_i32, _p, _p, _p]),
     "fgs_gather_rows": (C.c_int, [_i64, _i64, _p, _i32, _p, _p, _p, _p]),

@@ -31,7 +31,7 @@ BLOCK = 16
 __all__ = [
     "preprocess_forward", "binning_forward", "sort_keys", "tile_prep_forward", "rasterize_forward",
     "rasterize_gaussians", "rasterize_gaussians_forward", "preprocess_backward",
-    "rasterize_backward", "tile_grid", "sort_key_bits",
+    "rasterize_backward", "tile_grid", "sort_key_bits", "sort_status",
 ]
 
 
@@ -100,6 +100,10 @@ class _Workspace:
                 b = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
                 self._bufs[key] = b
             return b
+
+    def peek(self, dev: torch.device, tag: str) -> torch.Tensor | None:
+        with self._lock:
+            return self._bufs.get((dev.index, tag))
 
 
 _WS = _Workspace()
@@ -335,9 +339,12 @@ def binning_forward(xys, depths, point_offsets, conic_opacity, tiles_touched, mu
 
 
 def sort_keys(keys: torch.Tensor, values: torch.Tensor, num_tiles: int | None = None,
-              key_bits: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+              key_bits: int | None = None, check_status: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
     """Stable ascending sort of uint64 keys with their uint32 values (the
-    mx::argsort + take of binding.cpp:195-197) by the onesweep radix sort."""
+    mx::argsort + take of binding.cpp:195-197) by the onesweep radix sort.
+    check_status synchronises and raises RuntimeError if a bounded look-back
+    wait gave up (fgs_sort_status); without it the sort stays asynchronous
+    and ``sort_status(keys.device)`` reports later."""
     dev = keys.device
     k = keys.numel()
     if key_bits is None:
@@ -349,7 +356,18 @@ def sort_keys(keys: torch.Tensor, values: torch.Tensor, num_tiles: int | None = 
         ws = _WS.get(dev, "sort", nbytes)
         check(lib().fgs_sort_pairs(k, int(key_bits), _p(keys.contiguous()), _p(values.contiguous()),
                                    _p(ko), _p(vo), _p(ws), ws.numel(), _stream(dev)), "sort_keys")
+        if check_status:
+            sort_status(dev)
     return ko, vo
+
+
+def sort_status(dev) -> None:
+    """Synchronise and raise RuntimeError if the last sort_keys on ``dev``
+    had a look-back wait give up (its output is then undefined)."""
+    dev = torch.device(dev)
+    ws = _WS.peek(dev, "sort")
+    if ws is not None:  # no sort has run on dev otherwise
+        check(lib().fgs_sort_status(_p(ws), _stream(dev)), "sort_keys")
 
 
 def _tile_prep(keys, num_rendered, num_tiles, dev):
@@ -566,9 +584,11 @@ def rasterize_gaussians(inputs: dict, image_width: int, image_height: int, block
         b = binning_forward(pre["xys"], pre["depths"], point_offsets, pre["conic_opacity"],
                             pre["tiles_touched"], mult, gx, gy, 1, num_rendered)
         point_list_keys, point_list = sort_keys(b["point_list_keys_unsorted"],
-                                                b["point_list_unsorted"], num_tiles=T)
+                                                b["point_list_unsorted"], num_tiles=T,
+                                                check_status=False)
         ranges, bucket_count, bucket_offsets, bsum = _tile_prep(point_list_keys, num_rendered, T, dev)
         bucket_sum = int(bsum.item())  # host sync #2, as binding.cpp:212
+        sort_status(dev)  # the stream is idle now: reads the sort's timeout flag
         if bucket_sum > 0:
             ras = rasterize_forward(ranges, point_list, bucket_offsets, pre["xys"], pre["rgb"],
                                     pre["conic_opacity"], inputs["background"], pre["radii"],

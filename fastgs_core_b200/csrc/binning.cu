@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(kSortThreads)
                     uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
                     int shift, const uint32_t* __restrict__ digit_offsets,
                     uint32_t* __restrict__ lookback, uint32_t* __restrict__ counter,
-                    int* __restrict__ err) {
+                    int* __restrict__ err, int spin_limit, int withhold_first) {
   __shared__ uint32_t s_part;
   __shared__ uint32_t s_whist[kSortWarps][kRadix];  // per-warp digit counts -> warp offsets
   __shared__ uint32_t s_local_start[kRadix];
@@ -196,10 +196,13 @@ __global__ void __launch_bounds__(kSortThreads)
   const uint32_t real_cnt = (d == kRadix - 1) ? cnt - pads : cnt;
   // publish this partition's aggregate as early as possible
   uint32_t* lb = lookback + (size_t)part * kRadix + d;
-  if (part == 0)
-    st_volatile(lb, kFlagPrefix | real_cnt);
-  else
+  if (part == 0) {
+    // (test hook) withhold_first: partition 0 publishes nothing, so its
+    // successor's bounded wait runs out and reports FGS_ERR_TIMEOUT
+    if (!withhold_first) st_volatile(lb, kFlagPrefix | real_cnt);
+  } else {
     st_volatile(lb, kFlagAgg | real_cnt);
+  }
   // CTA-local exclusive scan over digits (for the shared-memory sort)
   {
     uint32_t x = cnt;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(kSortThreads)
       j -= used;
       if (used < kLookWindow && j >= 0) {
         // the predecessor at j has published nothing yet: wait and re-read
-        if (++spins > kSpinLimit) {
+        if (++spins > spin_limit) {
           atomicExch(err, 1);
           break;
         }
@@ -400,6 +403,11 @@ __global__ void __launch_bounds__(1024)
 }
 
 static inline int sort_passes(int key_bits) { return (key_bits + 7) / 8; }
+
+// Test hooks of the look-back wait (fgs_sort_set_test_hooks); the defaults
+// are the production values.
+static int g_spin_limit = kSpinLimit;
+static int g_withhold_first = 0;
 static inline int64_t sort_parts(int64_t n) { return (n + kPart - 1) / kPart; }
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -453,10 +461,10 @@ size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits) {
   const int passes = sort_passes(key_bits);
   const int64_t parts = sort_parts(num_rendered > 0 ? num_rendered : 1);
   size_t b = 0;
+  b += align256(4);                                         // timeout flag (offset 0)
   b += align256((size_t)passes * kRadix * 4);               // hist
   b += align256((size_t)passes * parts * kRadix * 4);       // lookback
   b += align256((size_t)passes * 4);                        // counters
-  b += align256(4);                                         // err
   b += align256((size_t)(num_rendered > 0 ? num_rendered : 1) * 8);  // tmp keys
   b += align256((size_t)(num_rendered > 0 ? num_rendered : 1) * 4);  // tmp vals
   return b;
@@ -491,20 +499,20 @@ int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end
   static unsigned long long attr_done = 0;
   smem_attr_once(onesweep_kernel, kSortDynSmem, &attr_done);
   char* w = (char*)workspace;
+  int* err = (int*)w;  // offset 0: fgs_sort_status reads it
+  w += align256(4);
   uint32_t* hist = (uint32_t*)w;
   w += align256((size_t)passes * kRadix * 4);
   uint32_t* lookback = (uint32_t*)w;
   w += align256((size_t)passes * parts * kRadix * 4);
   uint32_t* counters = (uint32_t*)w;
   w += align256((size_t)passes * 4);
-  int* err = (int*)w;
-  w += align256(4);
   uint64_t* tmp_keys = (uint64_t*)w;
   w += align256((size_t)num_rendered * 8);
   uint32_t* tmp_vals = (uint32_t*)w;
   cudaStream_t s = (cudaStream_t)stream;
-  // hist .. err are contiguous: clear them in one memset
-  cudaMemsetAsync(hist, 0, (size_t)((char*)tmp_keys - (char*)hist), s);
+  // err .. counters are contiguous: clear them in one memset
+  cudaMemsetAsync(err, 0, (size_t)((char*)tmp_keys - (char*)err), s);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -522,7 +530,7 @@ int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end
     uint32_t* dv = to_out ? values_out : tmp_vals;
     onesweep_kernel<<<(unsigned)parts, kSortThreads, kSortDynSmem, s>>>(
         src_k, src_v, dk, dv, num_rendered, bit_begin + 8 * p, hist + p * kRadix,
-        lookback + (size_t)p * parts * kRadix, counters + p, err);
+        lookback + (size_t)p * parts * kRadix, counters + p, err, g_spin_limit, g_withhold_first);
     src_k = dk;
     src_v = dv;
   }
@@ -531,7 +539,7 @@ int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end
 
 size_t fgs_depth_order_workspace_bytes(int32_t n) {
   const int64_t m = n > 0 ? n : 1;
-  return align256((size_t)m * 8) * 2 + align256((size_t)m * 4) + fgs_sort_workspace_bytes(m, 32);
+  return fgs_sort_workspace_bytes(m, 32) + align256((size_t)m * 8) * 2 + align256((size_t)m * 4);
 }
 
 int fgs_depth_order(int32_t n, const float* depths, const uint32_t* tiles_touched, uint32_t* order,
@@ -541,17 +549,19 @@ int fgs_depth_order(int32_t n, const float* depths, const uint32_t* tiles_touche
   if (n == 0) return FGS_OK;
   FGS_CHECK_ARG(depths && tiles_touched && order && tiles_in_order && workspace, "missing pointer");
   FGS_CHECK_ARG(workspace_bytes >= fgs_depth_order_workspace_bytes(n), "depth order workspace too small");
-  char* w = (char*)workspace;
+  // the sort's workspace comes first, so that its timeout flag sits at
+  // offset 0 of this workspace too (fgs_sort_status)
+  const size_t sws = fgs_sort_workspace_bytes(n, 32);
+  char* sort_ws = (char*)workspace;
+  char* w = sort_ws + sws;
   uint64_t* keys = (uint64_t*)w;
   w += align256((size_t)n * 8);
   uint64_t* skeys = (uint64_t*)w;
   w += align256((size_t)n * 8);
   uint32_t* vals = (uint32_t*)w;
-  w += align256((size_t)n * 4);
-  const size_t sws = fgs_sort_workspace_bytes(n, 32);
   cudaStream_t s = (cudaStream_t)stream;
   depth_keys_kernel<<<(n + 255) / 256, 256, 0, s>>>(n, depths, keys, vals);
-  int st = fgs_sort_pairs_bits(n, 0, 32, keys, vals, skeys, order, w, sws, stream);
+  int st = fgs_sort_pairs_bits(n, 0, 32, keys, vals, skeys, order, sort_ws, sws, stream);
   if (st) return st;
   gather_u32_kernel<<<(n + 255) / 256, 256, 0, s>>>(n, tiles_touched, order, tiles_in_order);
   return check_launch("depth_order");
@@ -623,10 +633,10 @@ namespace fgs {
 constexpr int64_t kStaticSortMaxKeys = FGS_SORT_STATIC_MAX_KEYS;
 constexpr int64_t kStaticSortParts = (kStaticSortMaxKeys + kPart - 1) / kPart;
 constexpr size_t kStaticSortBytes =
+    256 +                                                                      // timeout flag
     ((size_t)kMaxPasses * kRadix * 4 + 255) / 256 * 256 +                     // digit histograms
     ((size_t)kMaxPasses * kStaticSortParts * kRadix * 4 + 255) / 256 * 256 +  // look-back
     ((size_t)kMaxPasses * 4 + 255) / 256 * 256 +                              // tickets
-    256 +                                                                      // timeout flag
     ((size_t)kStaticSortMaxKeys * 8 + 255) / 256 * 256 +                      // ping-pong keys
     ((size_t)kStaticSortMaxKeys * 4 + 255) / 256 * 256;                       // ping-pong values
 
@@ -683,4 +693,38 @@ extern "C" int fgs_sort_pairs_static(int64_t num_rendered, int32_t key_bits,
   // call do not matter; the key/value halves need no clearing.
   return fgs_sort_pairs(num_rendered, key_bits, keys_in, values_in, keys_out, values_out, scratch,
                         fgs::kStaticSortBytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Status of the last sort run in a workspace: its timeout flag is the int at
+// offset 0 (for the static sort, of the static scratch on the current device).
+extern "C" int fgs_sort_status(const void* workspace, void* stream) {
+  const void* flag = workspace;
+  if (flag == nullptr) {
+    void* scratch = nullptr;
+    const int st = fgs::sort_scratch_address(&scratch);
+    if (st != FGS_OK) return st;
+    flag = scratch;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  int host = 0;
+  cudaError_t e = cudaMemcpyAsync(&host, flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    fgs::set_error("sort_status: %s", cudaGetErrorString(e));
+    return FGS_ERR_CUDA;
+  }
+  if (host != 0) {
+    fgs::set_error("sort: a look-back wait gave up after its poll limit; the sorted output is "
+                   "undefined");
+    return FGS_ERR_TIMEOUT;
+  }
+  return FGS_OK;
+}
+
+extern "C" int fgs_sort_set_test_hooks(int32_t spin_limit, int32_t withhold_first_partition) {
+  FGS_CHECK_ARG(spin_limit >= 0, "spin_limit must be >= 0");
+  fgs::g_spin_limit = spin_limit > 0 ? spin_limit : fgs::kSpinLimit;
+  fgs::g_withhold_first = withhold_first_partition ? 1 : 0;
+  return FGS_OK;
 }

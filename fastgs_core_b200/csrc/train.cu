@@ -29,7 +29,12 @@ __global__ void activate_kernel(int64_t n, const float* __restrict__ flat, float
   // only when n is a multiple of 4
   const float* qp = flat + 55 * n + 4 * i;
   const float4 q = make_float4(qp[0], qp[1], qp[2], qp[3]);
-  const float inv = 1.0f / (sqrtf(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w) + 1e-8f);
+  // explicitly rounded (this file may contract multiply-adds): the same bits
+  // as the preprocess kernels' in-kernel activation
+  const float ss = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(q.x, q.x), __fmul_rn(q.y, q.y)),
+                                       __fmul_rn(q.z, q.z)),
+                             __fmul_rn(q.w, q.w));
+  const float inv = 1.0f / (sqrtf(ss) + 1e-8f);
   reinterpret_cast<float4*>(quats)[i] = make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
 }
 

@@ -227,6 +227,11 @@ class Trainer:
         self._k_stream = torch.cuda.Stream(device=self.dev)
         self._cam_host = torch.empty(35, dtype=torch.float32, pin_memory=True)
         self._views = 0
+        # look-back timeout flags of each view's two sorts (depth order, tile
+        # bits), copied back in a two-slot ring: the host reads a view's slot
+        # after the next view's key-count wait, which orders after the copies
+        self._sort_flags = torch.zeros((2, 2), dtype=torch.int32, pin_memory=True)
+        self._flag_views: list[int] = []
         # one view on one rank: Adam fused into the backward pass (no
         # gradient buffer round trip); the gradient buffer is then not written
         self.fuse_adam = os.environ.get("FGS_FUSE_ADAM", "1") != "0"
@@ -315,12 +320,15 @@ class Trainer:
         return C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
 
     def render_view(self, cam, target=None, accumulate=False, loss_out=None, loss_scale=1.0,
-                    fused_adam=False, stats=None, metric_map=None, metric_count=None):
+                    fused_adam=False, stats=None, metric_map=None, metric_count=None,
+                    sort_only=False):
         """Forward (and, with a target, loss + backward accumulated into the
         flat gradient buffer) of one view. Returns the image [3, H*W]. With
         fused_adam the backward pass applies the Adam step (of step number
         self.step_count) to the parameters directly instead of writing the
-        gradient buffer: for a step whose gradient is this one view's."""
+        gradient buffer: for a step whose gradient is this one view's.
+        sort_only stops after the binning sort (self.last_sorted holds the
+        sorted keys and values) and returns None."""
         L = lib()
         n, d, ws = self.n, self.dev, self.ws
         W, H = int(cam.width), int(cam.height)
@@ -418,14 +426,21 @@ class Trainer:
         if cap > 0:
             dup(cap, kp)
         k_ready.synchronize()  # the one host sync: K sizes the sort and the bucket arrays
+        self._check_sort_flags()  # every earlier view's flag copies have landed
         K = int(self.k_host.item())
         self.last_rendered = K
         if K > cap:
             cap = self._key_cap = K + K // 4 + 1024
             kp, sws_n, kbufs = key_buffers(cap)
             dup(cap, kp)
+        slot = self._sort_flags[(self._views - 1) % 2]
+        slot.zero_()
+        if self.depth_first:
+            slot[0:1].copy_(dws[:4].view(torch.int32), non_blocking=True)
         if K > 0:
             self._call("sort", L.fgs_sort_pairs_bits, K, sort_lo, kb, *kp, sws_n, st)
+            slot[1:2].copy_(kbufs[4][:4].view(torch.int32), non_blocking=True)
+        self._flag_views.append(self._views - 1)
         if target is not None:
             # the raster-gradient accumulators are zeroed on the side stream
             # while this stream sorts and renders (every earlier use of them
@@ -443,6 +458,8 @@ class Trainer:
         skeys, svals = kbufs[2][:K], kbufs[3][:K]
         self.last_sorted = (skeys, svals)
         self.launches += 2 + (kb - sort_lo + 7) // 8  # histogram, digit scan, one pass per digit
+        if sort_only:
+            return None
         ranges = ws.get("ranges", 2 * T, torch.uint32)
         bcount = ws.get("bcount", T, torch.uint32)
         boffs = ws.get("boffs", T, torch.uint32)
@@ -506,6 +523,22 @@ class Trainer:
                    _p(dconic), _p(dvs), _p(radii), _p(clamped), int(bool(accumulate)),
                    _p(self.grads), _p(self.step_stats), st)
         return img
+
+    def _check_sort_flags(self) -> None:
+        """Raise if a sort of an earlier view reported a look-back timeout
+        (the flag fgs_sort_status reads). Call only where the copies of those
+        flags are known to have landed."""
+        views, self._flag_views = self._flag_views, []
+        for v in views:
+            f = self._sort_flags[v % 2]
+            if int(f[0]) or int(f[1]):
+                raise RuntimeError(f"sort of view {v} failed (status {_lib.FGS_ERR_TIMEOUT}): a "
+                                   "look-back wait gave up after its poll limit")
+
+    def check_sort_status(self) -> None:
+        """Synchronise and raise if any sort since the last check timed out."""
+        torch.cuda.current_stream(self.dev).synchronize()
+        self._check_sort_flags()
 
     def global_stats(self) -> torch.Tensor:
         """Densification statistics over every rank's views (sum; max for the

@@ -123,8 +123,10 @@ FGS_API int fgs_duplicate_with_keys(int32_t n, float mult, int32_t tile_bounds_x
  * bits (32 depth bits + bits of the largest tile id). Inputs are not
  * modified. Replaces mx::argsort + 2x mx::take (fastgs_core/binding/binding.cpp:195-197).
  * `workspace` holds fgs_sort_workspace_bytes(num_rendered, key_bits) bytes.
- * FGS_ERR_TIMEOUT if a bounded look-back wait gave up (the outputs are then
- * undefined but every store stayed in bounds).
+ * The sort is asynchronous: a bounded look-back wait that gives up cannot
+ * fail the call itself. It sets the timeout flag of the workspace instead
+ * (the outputs are then undefined, but every store stayed in bounds), which
+ * fgs_sort_status reports as FGS_ERR_TIMEOUT.
  */
 FGS_API size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits);
 FGS_API int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,
@@ -138,6 +140,22 @@ FGS_API int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t
                                 const uint64_t* keys_in, const uint32_t* values_in,
                                 uint64_t* keys_out, uint32_t* values_out, void* workspace,
                                 size_t workspace_bytes, void* stream);
+
+/* Status of the last sort run in `workspace` (fgs_sort_pairs,
+ * fgs_sort_pairs_bits, or the depth ordering of fgs_depth_order, whose
+ * workspace starts with its sort's): synchronises `stream`, then returns
+ * FGS_ERR_TIMEOUT if a look-back wait of that sort gave up, FGS_OK otherwise.
+ * workspace == NULL reads the scratch of fgs_sort_pairs_static on the current
+ * device. The flag is the int32 at byte offset 0 of the workspace (nonzero =
+ * timed out), so a caller that synchronises anyway may instead copy those 4
+ * bytes back itself. */
+FGS_API int fgs_sort_status(const void* workspace, void* stream);
+
+/* Test hooks of the look-back wait, process-wide: spin_limit polls before a
+ * wait gives up (0 restores the default, 2^22), and withhold_first_partition
+ * != 0 makes the first partition publish nothing, so that the next one's
+ * wait runs out without any fault. Not for production use; not thread-safe. */
+FGS_API int fgs_sort_set_test_hooks(int32_t spin_limit, int32_t withhold_first_partition);
 
 /* Depth-first binning, the training path's replacement for sorting the K
  * duplicated (tile | depth) keys on all 32 + ceil(log2 T) bits: the n
@@ -175,7 +193,8 @@ FGS_API int fgs_duplicate_with_keys_ordered(int32_t n, float mult, int32_t tile_
  * call on each device looks the area up (make it before any stream capture).
  * Every call shares that one area: calls that overlap on the GPU (other
  * streams, other host threads) race and must be serialised by the caller.
- * Same arguments and results as fgs_sort_pairs otherwise.
+ * Same arguments and results as fgs_sort_pairs otherwise; fgs_sort_status
+ * with a NULL workspace reports the last call's look-back timeout flag.
  */
 #define FGS_SORT_STATIC_MAX_KEYS 1048576
 FGS_API int fgs_sort_pairs_static(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,

@@ -71,3 +71,21 @@ def test_static_sort_rejects_oversize(cuda_dev):
     st = L.fgs_sort_pairs_static(MAX_KEYS + 1, 45, None, None, None, None, None)
     assert st == _lib.FGS_ERR_CAPACITY
     assert b"at most" in L.fgs_last_error()
+
+
+def test_static_sort_allocates_nothing(cuda_dev):
+    # after a first call (which looks the scratch up), a full-size call leaves
+    # the device's free memory exactly where it was
+    keys, vals = _keys(MAX_KEYS, 3, cuda_dev)
+    _sort_static(keys, vals, 45)
+    ko, vo = torch.empty_like(keys), torch.empty_like(vals)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    L = _lib.lib()
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _lib.check(L.fgs_sort_pairs_static(MAX_KEYS, 45, _p(keys), _p(vals), _p(ko), _p(vo), st),
+               "sort_pairs_static")
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert L.fgs_sort_status(None, st) == _lib.FGS_OK
