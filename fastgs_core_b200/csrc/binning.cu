@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(kDupThreads)
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
   const int i = order ? (int)order[j] : j;
+  if ((unsigned)i >= (unsigned)n) return;
   const uint32_t cnt = tiles[i];
   if (cnt == 0u) return;
   const int64_t off0 = (j == 0) ? 0 : (int64_t)offsets[j - 1];
@@ -70,7 +71,9 @@ __global__ void depth_keys_kernel(int n, const float* __restrict__ depths,
 __global__ void gather_u32_kernel(int n, const uint32_t* __restrict__ src,
                                   const uint32_t* __restrict__ index, uint32_t* __restrict__ dst) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j < n) dst[j] = src[index[j]];
+  if (j >= n) return;
+  const uint32_t i = index[j];
+  dst[j] = i < (uint32_t)n ? src[i] : 0u;
 }
 
 // --------------------------------------------------------------------- sort
@@ -138,7 +141,8 @@ __global__ void __launch_bounds__(kSortThreads)
                     uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out, int64_t n,
                     int shift, const uint32_t* __restrict__ digit_offsets,
                     uint32_t* __restrict__ lookback, uint32_t* __restrict__ counter,
-                    int* __restrict__ err, int spin_limit, int withhold_first) {
+                    int* __restrict__ err, int spin_limit, int withhold_first,
+                    const uint32_t* __restrict__ vals_orig, uint32_t* __restrict__ done) {
   __shared__ uint32_t s_part;
   __shared__ uint32_t s_whist[kSortWarps][kRadix];  // per-warp digit counts -> warp offsets
   __shared__ uint32_t s_local_start[kRadix];
@@ -275,6 +279,26 @@ __global__ void __launch_bounds__(kSortThreads)
     if (dst < (uint64_t)n) {
       keys_out[dst] = key;
       vals_out[dst] = s_vals[j];
+    }
+  }
+  // Last pass only (done != NULL): the CTA that finishes last checks the
+  // timeout flag of every pass. After a timeout the arrangement is undefined
+  // (slots may be unwritten), so it replaces the output with a safe one: every
+  // key all ones (an invalid tile id, which tile prep skips: nothing renders)
+  // and the caller's values in input order (in range for any consumer that
+  // indexes with them).
+  if (done != nullptr) {
+    __shared__ bool s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (s_last && ld_volatile(reinterpret_cast<const uint32_t*>(err)) != 0u) {
+      __threadfence();
+      for (int64_t i = tid; i < n; i += kSortThreads) {
+        keys_out[i] = ~0ull;
+        vals_out[i] = vals_orig[i];
+      }
     }
   }
 }
@@ -464,7 +488,7 @@ size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits) {
   b += align256(4);                                         // timeout flag (offset 0)
   b += align256((size_t)passes * kRadix * 4);               // hist
   b += align256((size_t)passes * parts * kRadix * 4);       // lookback
-  b += align256((size_t)passes * 4);                        // counters
+  b += align256((size_t)(passes + 1) * 4);                  // tickets, done counter
   b += align256((size_t)(num_rendered > 0 ? num_rendered : 1) * 8);  // tmp keys
   b += align256((size_t)(num_rendered > 0 ? num_rendered : 1) * 4);  // tmp vals
   return b;
@@ -505,8 +529,8 @@ int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end
   w += align256((size_t)passes * kRadix * 4);
   uint32_t* lookback = (uint32_t*)w;
   w += align256((size_t)passes * parts * kRadix * 4);
-  uint32_t* counters = (uint32_t*)w;
-  w += align256((size_t)passes * 4);
+  uint32_t* counters = (uint32_t*)w;  // [passes] tickets, then the last pass's done counter
+  w += align256((size_t)(passes + 1) * 4);
   uint64_t* tmp_keys = (uint64_t*)w;
   w += align256((size_t)num_rendered * 8);
   uint32_t* tmp_vals = (uint32_t*)w;
@@ -530,7 +554,8 @@ int fgs_sort_pairs_bits(int64_t num_rendered, int32_t bit_begin, int32_t bit_end
     uint32_t* dv = to_out ? values_out : tmp_vals;
     onesweep_kernel<<<(unsigned)parts, kSortThreads, kSortDynSmem, s>>>(
         src_k, src_v, dk, dv, num_rendered, bit_begin + 8 * p, hist + p * kRadix,
-        lookback + (size_t)p * parts * kRadix, counters + p, err, g_spin_limit, g_withhold_first);
+        lookback + (size_t)p * parts * kRadix, counters + p, err, g_spin_limit, g_withhold_first,
+        values_in, p == passes - 1 ? counters + passes : nullptr);
     src_k = dk;
     src_v = dv;
   }
@@ -636,7 +661,7 @@ constexpr size_t kStaticSortBytes =
     256 +                                                                      // timeout flag
     ((size_t)kMaxPasses * kRadix * 4 + 255) / 256 * 256 +                     // digit histograms
     ((size_t)kMaxPasses * kStaticSortParts * kRadix * 4 + 255) / 256 * 256 +  // look-back
-    ((size_t)kMaxPasses * 4 + 255) / 256 * 256 +                              // tickets
+    ((size_t)(kMaxPasses + 1) * 4 + 255) / 256 * 256 +                        // tickets, done
     ((size_t)kStaticSortMaxKeys * 8 + 255) / 256 * 256 +                      // ping-pong keys
     ((size_t)kStaticSortMaxKeys * 4 + 255) / 256 * 256;                       // ping-pong values
 
@@ -715,8 +740,8 @@ extern "C" int fgs_sort_status(const void* workspace, void* stream) {
     return FGS_ERR_CUDA;
   }
   if (host != 0) {
-    fgs::set_error("sort: a look-back wait gave up after its poll limit; the sorted output is "
-                   "undefined");
+    fgs::set_error("sort: a look-back wait gave up after its poll limit; the output holds "
+                   "all-ones keys and the input values instead of the sorted pairs");
     return FGS_ERR_TIMEOUT;
   }
   return FGS_OK;

@@ -124,9 +124,11 @@ FGS_API int fgs_duplicate_with_keys(int32_t n, float mult, int32_t tile_bounds_x
  * modified. Replaces mx::argsort + 2x mx::take (fastgs_core/binding/binding.cpp:195-197).
  * `workspace` holds fgs_sort_workspace_bytes(num_rendered, key_bits) bytes.
  * The sort is asynchronous: a bounded look-back wait that gives up cannot
- * fail the call itself. It sets the timeout flag of the workspace instead
- * (the outputs are then undefined, but every store stayed in bounds), which
- * fgs_sort_status reports as FGS_ERR_TIMEOUT.
+ * fail the call itself. It sets the timeout flag of the workspace instead,
+ * which fgs_sort_status reports as FGS_ERR_TIMEOUT, and the output is then
+ * not sorted but safe for the consumers: every stored key is all ones (an
+ * invalid tile id, so tile prep finds every tile empty) and the values are
+ * values_in in input order. Every store stays in bounds.
  */
 FGS_API size_t fgs_sort_workspace_bytes(int64_t num_rendered, int32_t key_bits);
 FGS_API int fgs_sort_pairs(int64_t num_rendered, int32_t key_bits, const uint64_t* keys_in,
