@@ -242,6 +242,83 @@ def run_other_config(args, S, Trainer, world, rank, local, dev, pg, warmup):
     return 0
 
 
+def api_e2e(scene, cams, host_targets, steps, warmup, dev):
+    """The drop-in path a caller of the reference's API runs, timed end to
+    end on one GPU: raw parameters as torch leaves, the trainers'
+    activations in torch, ``fastgs_core.rasterize_gaussians`` (with its two
+    host reads of K and the bucket count, as the reference's binding makes),
+    the fused L1 + D-SSIM loss, ``loss.backward()``, a fused torch Adam step
+    over the six parameter groups, the target copied from pinned host memory
+    and the loss read back every step. Returns (views/s, ms per step)."""
+    import torch
+
+    import fastgs_core as fc
+
+    raw = {k: torch.from_numpy(np.ascontiguousarray(getattr(scene, k))).to(dev).requires_grad_(True)
+           for k in ("means3d", "features_dc", "features_rest", "opacity_logits", "log_scales",
+                     "rotations")}
+    lrs = {"means3d": 3e-3, "features_dc": 1e-3, "features_rest": 1e-3 / 20.0,
+           "opacity_logits": 1e-3, "log_scales": 1e-3, "rotations": 1e-3}
+    opt = torch.optim.Adam([{"params": [raw[k]], "lr": lrs[k]} for k in raw], betas=(0.9, 0.99),
+                           eps=1e-8, fused=True)
+    W, H = cams[0].width, cams[0].height
+    dcams = [{"viewmatrix": torch.from_numpy(c.viewmatrix).to(dev),
+              "projmatrix": torch.from_numpy(c.projmatrix).to(dev),
+              "campos": torch.from_numpy(c.campos).to(dev)} for c in cams]
+    bg = torch.zeros(3, device=dev)
+    mm = torch.zeros(W * H, dtype=torch.int32, device=dev)
+    vs = torch.zeros((scene.n, 4), device=dev, requires_grad=True)
+    loss_host = torch.empty(1, pin_memory=True)
+    # the next step's target is copied on a side stream while this step runs
+    copy_stream = torch.cuda.Stream(device=dev)
+    cur = torch.cuda.current_stream(dev)
+    tbuf = [torch.empty((3, H, W), device=dev) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    for e in freed:
+        e.record(cur)
+
+    def prefetch(i):
+        k = i % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(freed[k])
+            tbuf[k].view(-1).copy_(host_targets[i % len(cams)].view(-1), non_blocking=True)
+            ready[k].record(copy_stream)
+
+    def step(i):
+        v = i % len(cams)
+        if i == 0:
+            prefetch(0)
+        prefetch(i + 1)
+        cur.wait_event(ready[i % 2])
+        tgt = tbuf[i % 2]
+        q = raw["rotations"]
+        ins = dict(means3d=raw["means3d"], dc=raw["features_dc"], sh=raw["features_rest"],
+                   opacities=torch.sigmoid(raw["opacity_logits"]), scales=torch.exp(raw["log_scales"]),
+                   rotations=q / (q.norm(dim=1, keepdim=True) + 1e-8), background=bg, metric_map=mm,
+                   viewspace_points=vs, **dcams[v])
+        out = fc.rasterize_gaussians(ins, W, H, 16, 16, cams[v].tan_fovx, cams[v].tan_fovy, 3)
+        loss = fc.l1_dssim_loss(out["out_color"].view(3, H, W), tgt)
+        opt.zero_grad(set_to_none=True)
+        vs.grad = None
+        loss.backward()
+        opt.step()
+        freed[i % 2].record(cur)
+        loss_host.copy_(loss.detach().view(1), non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(warmup, warmup + steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return 1000.0 / ms, ms
+
+
 def _emit(line: dict) -> None:
     """Print the one JSON result line on the real standard output."""
     sys.stdout.flush()
@@ -444,6 +521,13 @@ def main():
                     "d2h_bytes_per_step": 16},
             "clocks": clk,
         }
+        if world == 1:
+            # the reference's own call sequence through the drop-in API
+            api_v, api_ms = api_e2e(scene, cams, host_targets, min(args.steps, 100), warmup, dev)
+            line["e2e_api"] = {"value": api_v, "unit": "views/s", "ms_per_step": api_ms,
+                               "h2d_bytes_per_step": 3 * P * 4, "d2h_bytes_per_step": 4,
+                               "path": "fastgs_core.rasterize_gaussians + l1_dssim_loss + "
+                                       "backward + torch Adam (fused)"}
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(1)
         _emit(line)

@@ -6,6 +6,7 @@ argument names, dict schemas and errors); kernels are in libfastgs_b200.so
 """
 from .api import (  # noqa: F401
     binning_forward,
+    l1_dssim_loss,
     preprocess_backward,
     preprocess_forward,
     rasterize_backward,
@@ -14,6 +15,7 @@ from .api import (  # noqa: F401
     rasterize_gaussians_forward,
     sort_key_bits,
     sort_keys,
+    sort_status,
     tile_grid,
     tile_prep_forward,
 )

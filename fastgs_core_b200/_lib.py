@@ -30,7 +30,7 @@ class PreprocessParams(C.Structure):
 class RasterParams(C.Structure):
     _fields_ = [("image_width", _i32), ("image_height", _i32), ("num_tiles", _i32),
                 ("bucket_sum", _i64), ("num_gaussians", _i32), ("get_flag", _i32),
-                ("tile_order", _p), ("contrib_mask", _p)]
+                ("tile_order", _p), ("contrib_mask", _p), ("sparse_samples", _i32)]
 
 
 # name -> (restype, argtypes)

@@ -31,7 +31,7 @@ BLOCK = 16
 __all__ = [
     "preprocess_forward", "binning_forward", "sort_keys", "tile_prep_forward", "rasterize_forward",
     "rasterize_gaussians", "rasterize_gaussians_forward", "preprocess_backward",
-    "rasterize_backward", "tile_grid", "sort_key_bits", "sort_status",
+    "rasterize_backward", "tile_grid", "sort_key_bits", "sort_status", "l1_dssim_loss",
 ]
 
 
@@ -174,6 +174,7 @@ class _PreprocessFn(torch.autograd.Function):
                 cov3d_precomp, viewspace_points):
         dev = means3d.device
         o = _run_preprocess(prm, tensors, dev)
+        ctx.set_materialize_grads(False)  # unused outputs' cotangents stay None (no zero fills)
         ctx.prm = prm
         ctx.tensors = tensors
         ctx.fwd = {k: o[k] for k in ("cov3d", "radii", "clamped")}
@@ -412,13 +413,20 @@ def _run_rasterize(rp: RasterParams, t: dict, dev) -> dict:
     )
     mc = t["metric_count"]
     o["metric_count"] = (torch.empty_like(mc) if rp.get_flag else torch.zeros_like(mc))
-    # bucket_to_tile is declared [B*256] but only the first B entries are
-    # written (fastgs_rasterize.metal:67-75); the rest stay at the zero fill
-    if B:
-        o["bucket_to_tile"][B:].zero_()
-    # heaviest tiles first (same results in any order)
-    order = torch.empty(rp.num_tiles, dtype=torch.uint32, device=dev)
-    check(lib().fgs_tile_order(rp.num_tiles, _p(t["ranges"]), _p(order), _stream(dev)), "tile_order")
+    if "_tile_order" in t:
+        # rasterize_gaussians: bucket arrays sized by a bound on the bucket
+        # count, bucket_to_tile and the tile order written by tile prep; the
+        # caller trims the outputs to the real count once it is known
+        o["bucket_to_tile"] = t["_bucket_to_tile"]
+        order = t["_tile_order"]
+    else:
+        # bucket_to_tile is declared [B*256] but only the first B entries are
+        # written (fastgs_rasterize.metal:67-75); the rest stay at the zero fill
+        if B:
+            o["bucket_to_tile"][B:].zero_()
+        # heaviest tiles first (same results in any order)
+        order = torch.empty(rp.num_tiles, dtype=torch.uint32, device=dev)
+        check(lib().fgs_tile_order(rp.num_tiles, _p(t["ranges"]), _p(order), _stream(dev)), "tile_order")
     rp.tile_order = order.data_ptr() if rp.num_tiles else None
     # per (bucket, pixel) contributing-splat bits: the backward pass of this
     # autograd node reads them instead of re-deciding every pair
@@ -435,10 +443,12 @@ def _run_rasterize(rp: RasterParams, t: dict, dev) -> dict:
 
 def _run_rasterize_backward(rp: RasterParams, t: dict, o: dict, dout: torch.Tensor, dev) -> dict:
     n = t["means2d"].shape[0]
-    g = dict(dmeans2d=torch.zeros((n, 2), dtype=torch.float32, device=dev),
-             dcolors=torch.zeros((n, 3), dtype=torch.float32, device=dev),
-             dconic=torch.zeros((n, 4), dtype=torch.float32, device=dev),
-             dviewspace=torch.zeros((n, 4), dtype=torch.float32, device=dev))
+    # the kernel accumulates: one zeroed allocation, each part 16-byte aligned
+    o1 = -(-2 * n // 4) * 4
+    o2 = o1 + -(-3 * n // 4) * 4
+    buf = torch.zeros(o2 + 8 * n, dtype=torch.float32, device=dev)
+    g = dict(dmeans2d=buf[:2 * n].view(n, 2), dcolors=buf[o1:o1 + 3 * n].view(n, 3),
+             dconic=buf[o2:o2 + 4 * n].view(n, 4), dviewspace=buf[o2 + 4 * n:].view(n, 4))
     st = lib().fgs_rasterize_backward(
         C.byref(rp), *[_p(t[k]) for k in ("ranges", "point_list", "bucket_offsets", "means2d",
                                           "colors", "conic_opacity", "background")],
@@ -457,6 +467,7 @@ class _RasterizeFn(torch.autograd.Function):
     def forward(ctx, rp, t, means2d, colors, conic_opacity, viewspace_points):
         dev = t["means2d"].device
         o = _run_rasterize(rp, t, dev)
+        ctx.set_materialize_grads(False)  # only out_color's cotangent is used
         ctx.rp = rp
         ctx.t = t
         ctx.o = o
@@ -535,7 +546,72 @@ def rasterize_backward(ranges, point_list, per_tile_bucket_offset, means2d, colo
                 d_viewspace_points=g["dviewspace"])
 
 
+# ------------------------------------------------------------------- loss
+class _L1DssimFn(torch.autograd.Function):
+    """w_l1 * mean|image - target| + w_ssim * (1 - mean SSIM) with its
+    gradient from one fused pass (fgs_l1_dssim_loss)."""
+
+    @staticmethod
+    def forward(ctx, image, target, w_l1, w_ssim):
+        dev = image.device
+        if image.dim() != 3 or image.shape[0] != 3 or target.shape != image.shape:
+            raise ValueError("l1_dssim_loss expects image and target of shape (3, H, W)")
+        H, W = int(image.shape[1]), int(image.shape[2])
+        img = _f32(image, dev)
+        tgt = _f32(target, dev)
+        out = torch.empty(4, dtype=torch.float32, device=dev)
+        dimg = torch.empty_like(img)
+        scr = _WS.get(dev, "loss", int(lib().fgs_loss_scratch_bytes(W, H)))
+        check(lib().fgs_l1_dssim_loss(W, H, _p(img), _p(tgt), float(w_l1), float(w_ssim), _p(out),
+                                      _p(dimg), _p(scr), _stream(dev)), "l1_dssim_loss")
+        ctx.save_for_backward(dimg)
+        return out[0]
+
+    @staticmethod
+    def backward(ctx, g):
+        (dimg,) = ctx.saved_tensors
+        return dimg * g, None, None, None
+
+
+def l1_dssim_loss(image: torch.Tensor, target: torch.Tensor, w_l1: float = 1.0,
+                  w_ssim: float = 0.2) -> torch.Tensor:
+    """The training loss of the FastGS trainers with the D-SSIM term
+    (scripts/train_scanner_fastgs.py:949-964): w_l1 * mean |image - target| +
+    w_ssim * (1 - mean SSIM), SSIM with an 11x11 Gaussian window (sigma 1.5)
+    and zero padding. image, target: (3, H, W) float32 CUDA tensors; the
+    result is a differentiable scalar w.r.t. image."""
+    return _L1DssimFn.apply(image, target, w_l1, w_ssim)
+
+
 # ------------------------------------------------------ rasterize_gaussians
+_DUP_CAP: dict = {}  # device index -> key capacity of the duplicate buffers
+_HOST: dict = {}
+
+
+def _dup_buffers(dev, cap: int):
+    k = _WS.get(dev, "dup_keys", cap * 8)[:cap * 8].view(torch.uint64)
+    v = _WS.get(dev, "dup_vals", cap * 4)[:cap * 4].view(torch.uint32)
+    return k, v
+
+
+def _duplicate_into(pre, point_offsets, mult, gx, gy, n, cap, dev) -> None:
+    keys, vals = _dup_buffers(dev, cap)
+    check(lib().fgs_duplicate_with_keys(
+        n, float(mult), gx, gy, _p(pre["xys"]), _p(pre["depths"]), _p(point_offsets),
+        _p(pre["conic_opacity"]), _p(pre["tiles_touched"]), cap, _p(keys), _p(vals),
+        _stream(dev)), "binning_forward")
+
+
+def _host_slots(dev):
+    """Pinned slots for the bucket total and the sort flag, and their event."""
+    h = _HOST.get(dev.index)
+    if h is None:
+        h = _HOST[dev.index] = (torch.empty(1, dtype=torch.int64, pin_memory=True),
+                                torch.empty(1, dtype=torch.int32, pin_memory=True),
+                                torch.cuda.Event())
+    return h
+
+
 def rasterize_gaussians(inputs: dict, image_width: int, image_height: int, block_x: int = 16,
                         block_y: int = 16, tan_fovx: float = 1.0, tan_fovy: float = 1.0,
                         degree: int = 0, scale_modifier: float = 1.0, mult: float = 1.0,
@@ -566,6 +642,12 @@ def rasterize_gaussians(inputs: dict, image_width: int, image_height: int, block
     gx, gy = tile_grid(W, H)
     T = gx * gy
     point_offsets, total = _scan(pre["tiles_touched"], dev)
+    # duplicate-with-keys runs before the host knows K, into per-device
+    # grow-only buffers of the capacity earlier calls needed (its writes stop
+    # at the capacity); the sort reads them into fresh outputs
+    cap = _DUP_CAP.get(dev.index, 0)
+    if n and cap:
+        _duplicate_into(pre, point_offsets, mult, gx, gy, n, cap, dev)
     num_rendered = int(total.item()) if n else 0  # host sync #1, as binding.cpp:154
     res = {"rendered": num_rendered, "num_buckets": 0}
     empty_f = torch.zeros(0, dtype=torch.float32, device=dev)
@@ -581,19 +663,57 @@ def rasterize_gaussians(inputs: dict, image_width: int, image_height: int, block
                metric_count=metric_count)
     bucket_sum = 0
     if num_rendered > 0:
-        b = binning_forward(pre["xys"], pre["depths"], point_offsets, pre["conic_opacity"],
-                            pre["tiles_touched"], mult, gx, gy, 1, num_rendered)
-        point_list_keys, point_list = sort_keys(b["point_list_keys_unsorted"],
-                                                b["point_list_unsorted"], num_tiles=T,
-                                                check_status=False)
-        ranges, bucket_count, bucket_offsets, bsum = _tile_prep(point_list_keys, num_rendered, T, dev)
-        bucket_sum = int(bsum.item())  # host sync #2, as binding.cpp:212
-        sort_status(dev)  # the stream is idle now: reads the sort's timeout flag
-        if bucket_sum > 0:
-            ras = rasterize_forward(ranges, point_list, bucket_offsets, pre["xys"], pre["rgb"],
-                                    pre["conic_opacity"], inputs["background"], pre["radii"],
-                                    inputs["metric_map"], metric_count, pre["viewspace_points"],
-                                    W, H, 16, 16, 3, T, bucket_sum, get_flag)
+        K = num_rendered
+        if K > cap:
+            cap = _DUP_CAP[dev.index] = K + K // 4 + 1024
+            _duplicate_into(pre, point_offsets, mult, gx, gy, n, cap, dev)
+        keys_u, vals_u = _dup_buffers(dev, cap)
+        st = _stream(dev)
+        kb = sort_key_bits(T)
+        point_list_keys = torch.empty(K, dtype=torch.uint64, device=dev)
+        point_list = torch.empty(K, dtype=torch.uint32, device=dev)
+        nbytes = int(lib().fgs_sort_workspace_bytes(K, kb))
+        sws = _WS.get(dev, "sort", nbytes)
+        check(lib().fgs_sort_pairs(K, kb, _p(keys_u), _p(vals_u), _p(point_list_keys), _p(point_list),
+                                   _p(sws), sws.numel(), st), "sort_keys")
+        # tile prep with the bucket arrays sized by a bound (every tile has at
+        # most n_t/32 + 1 buckets); the bucket total and the sort's timeout
+        # flag go to the host on an event while the forward pass renders
+        Bmax = (K + 31) // 32 + T
+        ranges = torch.empty((T, 2), dtype=torch.uint32, device=dev)
+        bucket_count = torch.empty(T, dtype=torch.uint32, device=dev)
+        bucket_offsets = torch.empty(T, dtype=torch.uint32, device=dev)
+        bsum = torch.empty(1, dtype=torch.uint64, device=dev)
+        order = torch.empty(T, dtype=torch.uint32, device=dev)
+        b2t = torch.empty(Bmax * 256, dtype=torch.uint32, device=dev)
+        check(lib().fgs_tile_prep_ordered(K, T, _p(point_list_keys), _p(ranges), _p(bucket_count),
+                                          _p(bucket_offsets), _p(bsum), _p(order), _p(b2t), Bmax, st),
+              "tile_prep")
+        hb, hf, ev = _host_slots(dev)
+        hb.copy_(bsum.view(torch.int64), non_blocking=True)
+        hf.copy_(sws[:4].view(torch.int32), non_blocking=True)
+        ev.record(torch.cuda.current_stream(dev))
+        t = _raster_tensors(ranges, point_list, bucket_offsets, pre["xys"], pre["rgb"],
+                            pre["conic_opacity"], inputs["background"], inputs["metric_map"],
+                            metric_count, dev)
+        t["_tile_order"], t["_bucket_to_tile"] = order, b2t
+        rp = RasterParams(W, H, T, Bmax, int(t["metric_count"].numel()), int(bool(get_flag)))
+        outs = _RasterizeFn.apply(rp, t, pre["xys"], pre["rgb"], pre["conic_opacity"],
+                                  pre["viewspace_points"])
+        ev.synchronize()  # host read #2, as binding.cpp:212: the forward pass keeps running
+        bucket_sum = int(hb[0])
+        if int(hf[0]):
+            raise RuntimeError(f"sort_keys failed (status {_lib.FGS_ERR_TIMEOUT}): a look-back "
+                               "wait gave up after its poll limit")
+        # the backward pass walks the real buckets only
+        rp.bucket_sum = bucket_sum
+        ras = dict(zip(_RAS_OUT, outs))
+        B256 = bucket_sum * 256
+        ras["bucket_to_tile"] = b2t[:B256]
+        # declared [B*256], only the first B written (fastgs_rasterize.metal:67-75)
+        b2t[bucket_sum:B256].zero_()
+        ras["sampled_t"] = ras["sampled_t"][:B256]
+        ras["sampled_ar"] = ras["sampled_ar"].view(-1)[:3 * B256].view(3, B256)
     res["num_buckets"] = bucket_sum
     res.update({
         "out_color": ras["out_color"], "radii": pre["radii"], "point_offsets": point_offsets,

@@ -32,6 +32,7 @@ struct FwdArgs {
   const int32_t* metric_map;
   const uint32_t* tile_order;
   uint32_t* contrib_mask;  // optional [bucket][256]: contributing splats of the bucket per pixel
+  int sparse;              // samples of pixels terminated before a bucket are not written
   uint32_t* bucket_to_tile;
   float* sampled_t;
   float* sampled_ar;
@@ -151,15 +152,17 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
       bool any = false;
 #pragma unroll
       for (int k = 0; k < PX; ++k) {
-        a.sampled_t[b * kTile + lpix[k]] = done[k] ? 0.0f : T[k];
-        float* ar = a.sampled_ar + b * 3 * kTile + lpix[k];
-        ar[0] = done[k] ? 0.0f : C0[k];
-        ar[kTile] = done[k] ? 0.0f : C1[k];
-        ar[2 * kTile] = done[k] ? 0.0f : C2[k];
+        if (!(done[k] && a.sparse)) {
+          a.sampled_t[b * kTile + lpix[k]] = done[k] ? 0.0f : T[k];
+          float* ar = a.sampled_ar + b * 3 * kTile + lpix[k];
+          ar[0] = done[k] ? 0.0f : C0[k];
+          ar[kTile] = done[k] ? 0.0f : C1[k];
+          ar[2 * kTile] = done[k] ? 0.0f : C2[k];
+        }
         any |= !done[k];
       }
       if (!any) {
-        if (kMask) {
+        if (kMask && !a.sparse) {
 #pragma unroll
           for (int k = 0; k < PX; ++k) a.contrib_mask[b * kTile + lpix[k]] = 0u;
         }
@@ -204,14 +207,16 @@ __global__ void __launch_bounds__(kTile / PX) raster_fwd_kernel(FwdArgs a) {
       }
       if (kMask) {
 #pragma unroll
-        for (int k = 0; k < PX; ++k) a.contrib_mask[b * kTile + lpix[k]] = msk[k];
+        for (int k = 0; k < PX; ++k)
+          if (!(a.sparse && msk[k] == 0u && done[k])) a.contrib_mask[b * kTile + lpix[k]] = msk[k];
       }
     }
     processed = batch + cnt;
     __syncthreads();
   }
   // buckets the CTA never reached (every pixel had terminated): zero samples
-  for (int bl = (processed + 31) >> 5; bl < nb; ++bl) {
+  // (sparse: left unwritten, the backward pass does not read them)
+  for (int bl = a.sparse ? nb : (processed + 31) >> 5; bl < nb; ++bl) {
     const size_t b = (size_t)bbm0 + bl;
 #pragma unroll
     for (int k = 0; k < PX; ++k) {
@@ -300,6 +305,7 @@ int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,
   a.metric_map = metric_map;
   a.tile_order = p->tile_order;
   a.contrib_mask = p->contrib_mask;
+  a.sparse = p->sparse_samples != 0;
   a.bucket_to_tile = bucket_to_tile;
   a.sampled_t = sampled_t;
   a.sampled_ar = sampled_ar;

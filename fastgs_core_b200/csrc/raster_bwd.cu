@@ -48,6 +48,7 @@ struct BwdArgs {
   const uint32_t* max_contrib;
   const float* pixel_colors;
   const uint32_t* contrib_mask;
+  int sparse;  // samples of pixels whose last contributor precedes the bucket are not read
   float* dmeans2d;
   float* dcolors;
   float* dconic;
@@ -263,8 +264,17 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
     {
       // bucket start: the forward sample of each pixel
       const size_t bucket = (size_t)(gb0 + bi);
+      const int bstart = 32 * s_blocal[bi];
 #pragma unroll
       for (int k = 0; k < PX; ++k) {
+        if (a.sparse && last[k] <= bstart) {
+          // no splat of this bucket contributes to the pixel: its sample was
+          // not written, and none of the values below is used
+          T[k] = 0.0f;
+          adot[k] = 0.0f;
+          msk[k] = 0u;
+          continue;
+        }
         T[k] = a.sampled_t[bucket * kTilePx + lpix[k]];
         const float* sar = a.sampled_ar + bucket * 3 * kTilePx + lpix[k];
         adot[k] = sar[0] * d0[k] + sar[kTilePx] * d1[k] + sar[2 * kTilePx] * d2[k] - pcd[k];
@@ -456,6 +466,7 @@ int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
   const int64_t groups = (p->bucket_sum + kGroupBuckets - 1) / kGroupBuckets;
   FGS_CHECK_ARG(groups <= 0x7fffffff, "too many buckets");
   a.contrib_mask = p->contrib_mask;
+  a.sparse = p->sparse_samples != 0;
   if (a.contrib_mask)
     raster_bwd_kernel<kBwdPixelsPerThread, true><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
   else

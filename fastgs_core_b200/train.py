@@ -218,6 +218,8 @@ class Trainer:
         self.record = set()
         # forward pass records contributing pairs for the backward pass
         self.contrib_mask = os.environ.get("FGS_CONTRIB_MASK", "1") != "0"
+        # bucket samples only where a pixel is still live (fgs_raster_params.sparse_samples)
+        self.sparse_samples = os.environ.get("FGS_SPARSE_SAMPLES", "1") != "0"
         self._key_cap = 0  # capacity of the grow-only key buffers
         self.depth_first = os.environ.get("FGS_DEPTH_FIRST", "1") != "0"
         self._k_ready = torch.cuda.Event()  # recorded after each view's key-count copy
@@ -486,7 +488,9 @@ class Trainer:
         # scripts/train_scanner_fastgs.py:313): metric_map [P] int32 in,
         # metric_count [n] int32 out
         get_flag = int(metric_map is not None)
-        rp = RasterParams(W, H, T, Bmax, n, get_flag, order.data_ptr(), cm_ptr)
+        # sparse samples: pixels that terminated before a bucket get no sample
+        # writes there, and the backward pass reads none
+        rp = RasterParams(W, H, T, Bmax, n, get_flag, order.data_ptr(), cm_ptr, int(self.sparse_samples))
         self._call("rasterize_forward", L.fgs_rasterize_forward, C.byref(rp), _p(ranges), _p(svals), _p(boffs), _p(xys), _p(rgb), _p(conic),
             _p(self.background), _p(metric_map), _p(b2t), _p(samp_t), _p(samp_ar), _p(final_t), _p(ncontrib),
             _p(maxc), _p(pixc), _p(img), _p(metric_count), st)

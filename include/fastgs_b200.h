@@ -261,6 +261,14 @@ typedef struct fgs_raster_params {
    * re-deciding it (the gradients then use the fast exponential). NULL on
    * both sides reproduces the reference's recomputation. */
   uint32_t* contrib_mask;
+  /* Nonzero: the forward pass writes the bucket samples (and mask words) of
+   * a pixel only while the pixel is live at the bucket's start, and leaves
+   * the entries of pixels that terminated earlier unwritten instead of
+   * zeroing them; the backward pass, given the same flag, does not read
+   * those entries (no splat of such a bucket contributes to the pixel).
+   * Zero keeps the reference's fully written layout. Same gradients either
+   * way. */
+  int32_t sparse_samples;
 } fgs_raster_params;
 
 FGS_API int fgs_rasterize_forward(const fgs_raster_params* p, const uint32_t* ranges,

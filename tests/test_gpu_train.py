@@ -277,3 +277,41 @@ def test_depth_first_binning_matches_full_sort(n, cuda_dev):
     assert torch.equal(k1, k2)
     assert torch.equal(v1, v2)
     assert torch.equal(i1, i2)
+
+
+@pytest.mark.parametrize("mask", [True, False])
+def test_sparse_samples_same_gradients(mask, cuda_dev):
+    """Sparse bucket samples (no writes or reads for pixels that terminated
+    before a bucket) give the same image and, within the atomic-order noise,
+    the same gradients as the fully written layout, with and without the
+    contribution mask."""
+    scene, cam = S.small_scene(41, 20_000, 3, 160, 128, log_scale_mu=-2.6, op_mu=1.5)
+    target = torch.rand(3 * 160 * 128, generator=torch.Generator().manual_seed(9)).to(cuda_dev)
+    out = []
+    for sparse in (True, False):
+        tr = Trainer(scene, cuda_dev)
+        tr.contrib_mask = mask
+        tr.sparse_samples = sparse
+        tr.activate()
+        tr.step_stats.zero_()
+        img = tr.render_view(cam, target).clone()
+        out.append((img, tr.grads.clone(), tr.step_stats.clone()))
+    (i1, g1, s1), (i2, g2, s2) = out
+    assert torch.equal(i1, i2)
+    assert rel_err(g1.cpu().numpy(), g2.cpu().numpy()) < 1e-5
+    assert rel_err(s1.cpu().numpy(), s2.cpu().numpy()) < 1e-5
+
+
+def test_l1_dssim_loss_autograd(cuda_dev):
+    """fastgs_core.l1_dssim_loss as an autograd function against the torch
+    fp32 reference (value and gradient)."""
+    g = torch.Generator(device="cpu").manual_seed(77)
+    img = torch.rand((3, 70, 90), generator=g).to(cuda_dev).requires_grad_(True)
+    tgt = torch.rand((3, 70, 90), generator=g).to(cuda_dev)
+    loss = fg.l1_dssim_loss(img, tgt) * 2.0
+    loss.backward()
+    x = img.detach().clone().requires_grad_(True)
+    ref = torch_l1_dssim(x, tgt) * 2.0
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < 1e-5 * max(1.0, abs(ref.item()))
+    assert rel_err(img.grad.cpu().numpy(), x.grad.cpu().numpy()) < 1e-4
