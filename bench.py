@@ -19,9 +19,11 @@ binning sort; keys/s) print one line for those BASELINE configurations
 instead; the default line is config 3.
 
 Printed JSON (rank 0): value = views/s of the whole job with parameters,
-targets and state resident in HBM; e2e = the same step through the public API
-with the target image copied from pinned host memory and the loss read back
-each step; roofline of the rasterize-backward kernel (the dominant kernel)
+targets and state resident in HBM; e2e = the same step through the training
+entry point (fastgs_core_b200.train.Trainer.step) with the target image copied
+from pinned host memory and the loss read back each step; e2e_api = the step a
+caller of the reference's API makes (rasterize_gaussians + loss + backward +
+torch Adam), also end to end; roofline of the rasterize-backward kernel (the dominant kernel)
 timed live with CUDA events; cpu_baseline = the same step on the host cores
 (C oracle + numpy, OpenMP over all cores) for one view.
 """
@@ -122,6 +124,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def _cpu_model() -> str:
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
 def cpu_baseline(steps: int = 1):
     """The same step (one view) on the host cores through the C oracle."""
     from fastgs_core_b200 import synthetic as S
@@ -137,6 +151,7 @@ def cpu_baseline(steps: int = 1):
         times.append(dt)
     t = float(np.mean(times))
     return {"value": 1.0 / t, "unit": "views/s", "cores": os.cpu_count(), "kind": "port",
+            "cpu_model": _cpu_model(), "omp_threads": os.cpu_count(),
             "sample": f"{steps} full config-3 training step(s) of one view on the host "
                       f"(C oracle fwd/bwd with OpenMP, numpy/scipy loss and Adam); "
                       f"{t:.2f} s per view"}
@@ -438,7 +453,7 @@ def main():
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms = float(t_max.item())
 
-    # ---------------- e2e: public API with host buffers every step
+    # ---------------- e2e: the Trainer's step with host buffers every step
     # the target of step s+1 is copied from pinned host memory on a copy
     # stream while step s computes (double buffer); the loss comes back each step
     loss_host = torch.empty(4, pin_memory=True)

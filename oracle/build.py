@@ -20,7 +20,15 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REF = "/root/reference"
+
+
+def default_reference_dir() -> str:
+    """The reference checkout: $FGS_REFERENCE_DIR, else a directory named
+    ``reference`` beside this repository's root."""
+    env = os.environ.get("FGS_REFERENCE_DIR")
+    if env:
+        return env
+    return os.path.normpath(os.path.join(HERE, os.pardir, os.pardir, "reference"))
 
 CFLAGS = ["-O2", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-std=c11"]
 
@@ -44,7 +52,8 @@ def build_oracle(force: bool = False) -> None:
             _run(["gcc", *CFLAGS, *extra, src, "-o", out, "-lm"])
 
 
-def build_ref(reference_dir: str = DEFAULT_REF, force: bool = False) -> bool:
+def build_ref(reference_dir: str | None = None, force: bool = False) -> bool:
+    reference_dir = reference_dir or default_reference_dir()
     metal_dir = os.path.join(reference_dir, "fastgs_core", "metal")
     if not os.path.isdir(metal_dir):
         return False
@@ -61,7 +70,8 @@ def build_ref(reference_dir: str = DEFAULT_REF, force: bool = False) -> bool:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-dir", default=DEFAULT_REF)
+    ap.add_argument("--reference-dir", default=None,
+                    help="reference checkout (default: $FGS_REFERENCE_DIR or ../reference)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     build_oracle(a.force)

@@ -209,3 +209,96 @@ def test_driver_schedule_runs(cuda_dev):
     assert any("final_prune" in o for o in outs)
     assert drv.active_sh_degree == 3
     assert tr.n != n
+
+
+# ---------------------------------------------------------------------------
+# Against fixtures made by the reference's own densification functions
+# (tests/golden/make_densify_golden.py; the CPU checker is pinned to the same
+# fixtures in tests/test_densify_golden.py).
+import json  # noqa: E402
+import os  # noqa: E402
+
+GOLD = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "densify_ref.npz")))
+
+
+def trainer_from_fixture(cuda_dev, tag):
+    z = GOLD
+    p = {k: z[f"{tag}_in_{k}"] for k in NAMES}
+    n = p["means3d"].shape[0]
+    scene = S.Scene(p["means3d"], p["features_dc"], p["features_rest"], p["opacity_logits"],
+                    p["log_scales"], p["rotations"], 3)
+    tr = Trainer(scene, cuda_dev)
+    m = np.concatenate([z[f"{tag}_in_m_{k}"].reshape(-1) for k in NAMES])
+    v = np.concatenate([z[f"{tag}_in_v_{k}"].reshape(-1) for k in NAMES])
+    tr.exp_avg[:59 * n] = torch.from_numpy(m).to(cuda_dev)
+    tr.exp_avg_sq[:59 * n] = torch.from_numpy(v).to(cuda_dev)
+    st = np.concatenate([z[f"{tag}_in_acc"], z[f"{tag}_in_acc_abs"], z[f"{tag}_in_denom"],
+                         z[f"{tag}_in_max_radii"]])
+    tr.stats.copy_(torch.from_numpy(st).to(cuda_dev))
+    return tr
+
+
+def compare_fixture(tr, prefix, approx=(), stats=True):
+    n = tr.n
+    got = split_flat(tr.params.cpu().numpy(), n)
+    gm = split_flat(tr.exp_avg[:59 * n].cpu().numpy(), n)
+    gv = split_flat(tr.exp_avg_sq[:59 * n].cpu().numpy(), n)
+    for k in NAMES:
+        want = GOLD[f"{prefix}_{k}"]
+        assert got[k].shape == want.shape, k
+        if k in approx:
+            np.testing.assert_allclose(got[k], want, rtol=1e-5, atol=1e-6, err_msg=k)
+        else:
+            assert np.array_equal(got[k], want), k
+        m_key = prefix.replace("_out", "_out_m").replace("_partial", "_partial_m")
+        v_key = prefix.replace("_out", "_out_v").replace("_partial", "_partial_v")
+        assert np.array_equal(gm[k], GOLD[f"{m_key}_{k}"]), k
+        assert np.array_equal(gv[k], GOLD[f"{v_key}_{k}"]), k
+    if stats:
+        s = tr.stats.cpu().numpy()
+        tag = prefix.split("_out")[0]
+        for i, zk in enumerate(("acc", "acc_abs", "denom", "max_radii")):
+            assert np.array_equal(s[i * n:(i + 1) * n], GOLD[f"{tag}_out_{zk}"]), zk
+
+
+@pytest.mark.parametrize("tag", ["clone_cap", "prune_cap"])
+def test_densify_and_prune_matches_reference_fixture(tag, cuda_dev):
+    tr = trainer_from_fixture(cuda_dev, tag)
+    args = D.DensifyArgs(**json.loads(str(GOLD[f"{tag}_args"])))
+    got = D.densify_and_prune_fastgs(tr, args, float(GOLD["extent"]), GOLD[f"{tag}_in_importance"],
+                                     GOLD[f"{tag}_in_pruning"],
+                                     np.random.default_rng(int(GOLD[f"{tag}_seed"])))
+    assert got == json.loads(str(GOLD[f"{tag}_result"]))
+    compare_fixture(tr, f"{tag}_out", approx=("opacity_logits",))
+
+
+def test_split_matches_reference_fixture(cuda_dev):
+    """The reference's split result (recorded where its bookkeeping raises
+    after the split was applied)."""
+    tag = "split"
+    tr = trainer_from_fixture(cuda_dev, tag)
+    args = D.DensifyArgs(**json.loads(str(GOLD[f"{tag}_args"])))
+    n = tr.n
+    st = GOLD
+    denom = np.maximum(st["split_in_denom"], 1.0)
+    q_abs = np.abs(st["split_in_acc_abs"] / denom) >= args.grad_abs_thresh
+    max_scale = np.max(np.exp(st["split_in_log_scales"]), axis=1)
+    metric = st["split_in_importance"] > args.importance_score_threshold
+    split_filter = (max_scale > args.dense * float(st["extent"])) & q_abs
+    count, children, _ = D.densify_and_split(tr, metric, split_filter,
+                                             np.random.default_rng(int(st["split_seed"])), 2)
+    assert count > 0 and tr.n == n + count
+    compare_fixture(tr, "split_partial", approx=("means3d", "log_scales"), stats=False)
+
+
+def test_final_prune_reset_prune_match_reference_fixture(cuda_dev):
+    tr = trainer_from_fixture(cuda_dev, "final_prune")
+    got = D.final_prune_fastgs(tr, 0.5, GOLD["final_prune_in_pruning"], 0.3, 200)
+    assert got == json.loads(str(GOLD["final_prune_result"]))
+    compare_fixture(tr, "final_prune_out")
+    tr = trainer_from_fixture(cuda_dev, "reset")
+    D.reset_opacity_logits(tr, 0.05)
+    compare_fixture(tr, "reset_out", approx=("opacity_logits",))
+    tr = trainer_from_fixture(cuda_dev, "prune")
+    D.prune_points(tr, GOLD["prune_mask"])
+    compare_fixture(tr, "prune_out")
