@@ -69,6 +69,7 @@ _SIGS = {
                                      + [_f, _f, _f, _i32, _i32, _p, _p]),
     "fgs_loss_scratch_bytes": (_sz, [_i32, _i32]),
     "fgs_l1_dssim_loss": (C.c_int, [_i32, _i32, _p, _p, _f, _f, _p, _p, _p, _p]),
+    "fgs_mse_loss": (C.c_int, [_i32, _i32, _p, _p, _f, _p, _p, _p, _p]),
     "fgs_adam_step": (C.c_int, [_i64, _p, _p, _p, _p, _i32, C.POINTER(_i64), C.POINTER(_f), _f, _f,
                                 _f, _i32, _i32, _p]),
     "fgs_adam_step_multicast": (C.c_int, [_i64, _p, _p, _p, _p, _p, _i32, C.POINTER(_i64),

@@ -287,6 +287,32 @@ __global__ void loss_finalize_kernel(const float* __restrict__ partials, int nbl
   }
 }
 
+// Mean squared error and its gradient (the reference trainer's warm-up loss):
+// one strided pass, a per-block partial of sum (x - y)^2 in partials[2 blk + 1]
+// (partials[2 blk] = 0: the SSIM slot loss_finalize_kernel also reads).
+__global__ void __launch_bounds__(256)
+    mse_kernel(int64_t n, const float* __restrict__ x, const float* __restrict__ y, float g_scale,
+               float* __restrict__ dimg, float* __restrict__ partials) {
+  __shared__ float s_w[8];
+  float acc = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float d = x[i] - y[i];
+    acc = fmaf(d, d, acc);
+    dimg[i] = g_scale * d;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int k = 0; k < 8; ++k) t += s_w[k];
+    partials[2 * blockIdx.x] = 0.0f;
+    partials[2 * blockIdx.x + 1] = t;
+  }
+}
+
 // -------------------------------------------------------------------- Adam
 struct AdamGroups {
   int64_t end[8];
@@ -558,6 +584,25 @@ int fgs_activate_params(int64_t n, const float* params_flat, float* opacities, f
 size_t fgs_loss_scratch_bytes(int32_t width, int32_t height) {
   const size_t blocks = (size_t)((width + kFO - 1) / kFO) * ((height + kFO - 1) / kFO) * 3;
   return (2 * blocks + 64) * sizeof(float);
+}
+
+int fgs_mse_loss(int32_t width, int32_t height, const float* image, const float* target, float w_mse,
+                 float* loss_out, float* dL_dimage, void* scratch, void* stream) {
+  FGS_CHECK_ARG(width > 0 && height > 0, "image size must be positive");
+  FGS_CHECK_ARG(image && target && loss_out && dL_dimage && scratch, "missing pointer");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t n = 3 * (int64_t)width * height;
+  // as many blocks as the fused L1 + D-SSIM pass (the scratch is sized for those)
+  const int64_t tiles = (int64_t)((width + kFO - 1) / kFO) * ((height + kFO - 1) / kFO) * 3;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int nblk = (int)(tiles < (int64_t)sms * 8 ? tiles : (int64_t)sms * 8);
+  const float inv_n = 1.0f / (float)n;
+  mse_kernel<<<nblk, 256, 0, s>>>(n, image, target, 2.0f * w_mse * inv_n, dL_dimage, (float*)scratch);
+  // out[0] = w_mse * mse, out[1] = mse, out[2] = 0
+  loss_finalize_kernel<<<1, 1024, 0, s>>>((const float*)scratch, nblk, w_mse, 0.0f, inv_n, loss_out);
+  return check_launch("mse_loss");
 }
 
 int fgs_l1_dssim_loss(int32_t width, int32_t height, const float* image, const float* target,

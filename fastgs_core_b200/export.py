@@ -4,9 +4,9 @@
   scripts/train_scanner_fixed.py:631-688): log-scales, opacity logits, dc
   and rest SH as stored, positions and rotations moved into the y-up frame
   of the Scaniverse preview ((x, y, z) -> (x, -z, y), rotations conjugated
-  by the same axis change); save_as_spz writes them through the `spz`
-  module when it is importable and otherwise returns False, as the
-  reference does;
+  by the same axis change), written by this module's own .spz encoder
+  (write_spz), since the reference's `spz` submodule (nianticlabs/spz,
+  .gitmodules:1-3) is not part of its tree; read_spz decodes the files;
 * the common 3DGS PLY layout (binary little endian; x y z, nx ny nz, f_dc_*,
   f_rest_* channel-major, opacity logit, scale_* (log), rot_* (w x y z)),
   written and read back.
@@ -80,21 +80,153 @@ def spz_cloud_arrays(params: dict) -> dict:
             "sh": params["features_rest"].reshape(-1).astype(np.float32)}
 
 
+# ------------------------------------------------------------------ .spz
+# The packed Gaussian format of nianticlabs/spz (version 2 of its published
+# layout): a gzip stream holding a 16-byte little-endian header
+#   uint32 magic 0x5053474e ("NGSP"), uint32 version, uint32 point count,
+#   uint8 SH degree, uint8 fractional bits, uint8 flags (1 = antialiased),
+#   uint8 reserved
+# followed by one block per attribute, points in order:
+#   positions  3 x 24-bit two's complement fixed point (round(x * 2^bits))
+#   alphas     uint8 round(sigmoid(logit) * 255)
+#   colors     3 x uint8 round(dc * 0.15 * 255 + 127.5)
+#   scales     3 x uint8 round((log_scale + 10) * 16)
+#   rotations  3 x uint8 of the unit quaternion (x, y, z, w) with w >= 0:
+#              round(v * 127.5 + 127.5) for x, y, z (w is recovered)
+#   sh         (coefficient, channel) x uint8 q = round(v * 128) + 128,
+#              rounded to buckets of 8 (the 9 values of degree 1) or 16
+#              (higher degrees)
+# uint8 quantities are clamped to [0, 255].
+SPZ_MAGIC = 0x5053474E
+SPZ_VERSION = 2
+SPZ_FRACTIONAL_BITS = 12
+_SPZ_COLOR_SCALE = 0.15
+
+
+def _round(x) -> np.ndarray:
+    """Round half away from zero (C's round / lround, which the format's
+    encoder uses), in float32 arithmetic like the encoder."""
+    x = np.asarray(x, np.float32)
+    return np.sign(x) * np.floor(np.abs(x) + np.float32(0.5))
+
+
+def _u8(x) -> np.ndarray:
+    return np.clip(_round(x), 0, 255).astype(np.uint8)
+
+
+def _sh_quantize(x, bucket: int) -> np.ndarray:
+    q = (_round(np.asarray(x, np.float32) * np.float32(128.0)) + 128.0).astype(np.int64)
+    q = (q + bucket // 2) // bucket * bucket
+    return np.clip(q, 0, 255).astype(np.uint8)
+
+
+def _sh_dim(degree: int) -> int:
+    return (degree + 1) ** 2 - 1
+
+
+def write_spz(filename, cloud: dict, sh_degree: int, antialiased: bool = True) -> None:
+    """Write the spz_cloud_arrays dictionary (flat float32 arrays of the
+    spz.GaussianCloud fields; rotations as given, read as x, y, z, w) to a
+    .spz file."""
+    import gzip
+    import struct
+
+    pos = np.asarray(cloud["positions"], np.float32).reshape(-1, 3)
+    n = pos.shape[0]
+    dim = _sh_dim(int(sh_degree))
+    sh = np.asarray(cloud.get("sh", np.zeros(0, np.float32)), np.float32).reshape(n, -1)
+    if sh.shape[1] < 3 * dim:
+        raise ValueError(f"sh holds {sh.shape[1] // 3} coefficients per point, degree {sh_degree} "
+                         f"needs {dim}")
+    sh = sh[:, :3 * dim]
+    f32 = np.float32
+    fixed = _round(pos * f32(1 << SPZ_FRACTIONAL_BITS)).astype(np.int64)
+    fixed = np.clip(fixed, -(1 << 23), (1 << 23) - 1) & 0xFFFFFF
+    pos_b = np.stack([(fixed >> (8 * k)) & 0xFF for k in range(3)], -1).astype(np.uint8)
+    logits = np.asarray(cloud["alphas"], f32).reshape(n)
+    alpha_b = _u8((f32(1.0) / (f32(1.0) + np.exp(-logits))) * f32(255.0))
+    color_b = _u8(np.asarray(cloud["colors"], f32).reshape(n, 3) * f32(_SPZ_COLOR_SCALE * 255.0)
+                  + f32(0.5 * 255.0))
+    scale_b = _u8((np.asarray(cloud["scales"], f32).reshape(n, 3) + f32(10.0)) * f32(16.0))
+    q = np.asarray(cloud["rotations"], f32).reshape(n, 4)
+    q = q / np.maximum(np.linalg.norm(q, axis=1, keepdims=True), f32(1e-30))
+    q = q * np.where(q[:, 3:4] < 0, f32(-127.5), f32(127.5)) + f32(127.5)
+    rot_b = _u8(q[:, :3])
+    sh_b = np.empty((n, 3 * dim), np.uint8)
+    k1 = min(9, 3 * dim)
+    sh_b[:, :k1] = _sh_quantize(sh[:, :k1], 8)
+    sh_b[:, k1:] = _sh_quantize(sh[:, k1:], 16)
+    header = struct.pack("<IIIBBBB", SPZ_MAGIC, SPZ_VERSION, n, int(sh_degree), SPZ_FRACTIONAL_BITS,
+                         1 if antialiased else 0, 0)
+    body = b"".join(a.tobytes() for a in (pos_b, alpha_b, color_b, scale_b, rot_b, sh_b))
+    with gzip.open(filename, "wb") as fh:
+        fh.write(header + body)
+
+
+def read_spz(filename) -> dict:
+    """Decode a .spz file (versions 2 and 3 of the packed layout) into the
+    spz_cloud_arrays fields plus sh_degree and antialiased."""
+    import gzip
+    import struct
+
+    with gzip.open(filename, "rb") as fh:
+        raw = fh.read()
+    magic, version, n, deg, bits, flags, _ = struct.unpack_from("<IIIBBBB", raw, 0)
+    if magic != SPZ_MAGIC:
+        raise ValueError(f"{filename}: not an spz file (magic {magic:#x})")
+    if version not in (2, 3):
+        raise ValueError(f"{filename}: unsupported spz version {version}")
+    dim = _sh_dim(deg)
+    off = 16
+
+    def take(count):
+        nonlocal off
+        a = np.frombuffer(raw, np.uint8, count, off)
+        off += count
+        return a
+
+    pb = take(9 * n).reshape(n, 3, 3).astype(np.int64)
+    fixed = pb[..., 0] | (pb[..., 1] << 8) | (pb[..., 2] << 16)
+    fixed = np.where(fixed & 0x800000, fixed - (1 << 24), fixed)
+    positions = (fixed / float(1 << bits)).astype(np.float32)
+    alphas_u = take(n).astype(np.float64) / 255.0
+    alphas = np.log(np.clip(alphas_u, 1e-6, 1 - 1e-6) / np.clip(1 - alphas_u, 1e-6, None))
+    colors = (take(3 * n).astype(np.float64) - 127.5) / (_SPZ_COLOR_SCALE * 255.0)
+    scales = take(3 * n).astype(np.float64) / 16.0 - 10.0
+    if version == 2:
+        xyz = take(3 * n).reshape(n, 3).astype(np.float64) / 127.5 - 1.0
+        w = np.sqrt(np.maximum(0.0, 1.0 - (xyz * xyz).sum(1, keepdims=True)))
+        rotations = np.concatenate([xyz, w], 1)
+    else:
+        # smallest three: 2 bits of the largest component, 3 x 10 bits (sign + 9)
+        packed = take(4 * n).reshape(n, 4).astype(np.uint32)
+        v = packed[:, 0] | (packed[:, 1] << 8) | (packed[:, 2] << 16) | (packed[:, 3] << 24)
+        largest = (v >> 30) & 3
+        rotations = np.zeros((n, 4))
+        mag_mask = (1 << 9) - 1
+        rest = v.copy()
+        sumsq = np.zeros(n)
+        for i in range(3, -1, -1):
+            sel = largest != i
+            mag = (rest & mag_mask).astype(np.float64)
+            neg = (rest >> 9) & 1
+            comp = np.sqrt(0.5) * mag / mag_mask * np.where(neg == 1, -1.0, 1.0)
+            rotations[sel, i] = comp[sel]
+            sumsq += np.where(sel, comp * comp, 0.0)
+            rest = np.where(sel, rest >> 10, rest)
+        rotations[np.arange(n), largest] = np.sqrt(np.maximum(0.0, 1.0 - sumsq))
+    sh = (take(3 * dim * n).astype(np.float64) - 128.0) / 128.0
+    return {"positions": positions.reshape(-1), "alphas": alphas.astype(np.float32),
+            "colors": colors.astype(np.float32).reshape(-1), "scales": scales.astype(np.float32).reshape(-1),
+            "rotations": rotations.astype(np.float32).reshape(-1), "sh": sh.astype(np.float32),
+            "sh_degree": int(deg), "antialiased": bool(flags & 1)}
+
+
 def save_as_spz(filename, tr, sh_degree: int) -> bool:
-    """save_as_spz (scripts/train_scanner_fixed.py:631-688) for a Trainer."""
-    try:
-        import spz  # noqa: PLC0415
-    except ImportError:
-        print("[WARN] spz is not available; skip final.spz export")
-        return False
-    a = spz_cloud_arrays(trainer_arrays(tr))
-    cloud = spz.GaussianCloud()
-    cloud.antialiased = True
-    for k, v in a.items():
-        setattr(cloud, k, v)
-    cloud.sh_degree = int(sh_degree)
-    if not spz.save_spz(cloud, spz.PackOptions(), str(filename)):
-        raise RuntimeError(f"failed to save spz to {filename}")
+    """save_as_spz (scripts/train_scanner_fixed.py:631-688) for a Trainer:
+    the same arrays, antialiased, through write_spz."""
+    write_spz(filename, spz_cloud_arrays(trainer_arrays(tr)), sh_degree, antialiased=True)
+    print(f"saved spz: {filename}")
     return True
 
 

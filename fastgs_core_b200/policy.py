@@ -5,11 +5,14 @@ decay, the optimiser cadence, staged parameter groups, the SH-degree ramp,
 view sampling without replacement, densification with FastGS scores, opacity
 resets and the final prune window.
 
+The loss follows the reference's: mean squared error up to step mse_until
+(its --mse-until, :824, 980), then the Trainer's L1 (the reference's is plain
+L1; the Trainer adds w_ssim * D-SSIM, 0 gives the reference's).
+
 Differences from the reference loop, by design: one render per step (its
 viewspace gradient feeds the densification statistics directly, where the
-reference renders a second time); the loss is Trainer's L1 (+ weighted
-D-SSIM) from the first step (the reference's MSE warm-up, --mse-until, is
-not built); best-image saving and logging are left to the caller.
+reference renders a second time); best-image saving and logging are left to
+the caller.
 """
 from __future__ import annotations
 
@@ -111,6 +114,7 @@ class DriverConfig:
     """The training loop's schedule (scripts/train_scanner_fastgs.py:820-849)."""
     sh_degree: int = 3
     sh_degree_interval: int = 1000
+    mse_until: int = 600
     stage_color_steps: int = 0
     stage_means_steps: int = 0
     stage_scales_steps: int = 0
@@ -185,6 +189,7 @@ class FastGSDriver:
         if step % c.sh_degree_interval == 0:
             self.active_sh_degree = min(self.active_sh_degree + 1, c.sh_degree)
         tr.sh_degree = self.active_sh_degree
+        tr.loss_mode = "l1_dssim" if step > c.mse_until else "mse"
         if not self.viewpoint_stack:
             self.viewpoint_stack = list(range(len(self.cameras)))
         idx = self.viewpoint_stack.pop(int(self.rng.integers(0, len(self.viewpoint_stack))))

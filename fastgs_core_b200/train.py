@@ -152,6 +152,9 @@ class Trainer:
         self.sh_degree = int(scene.sh_degree)
         self.lrs = lrs or LearningRates()
         self.w_l1, self.w_ssim = float(w_l1), float(w_ssim)
+        # "l1_dssim" (w_l1 L1 + w_ssim D-SSIM) or "mse" (the reference
+        # trainer's warm-up loss, scripts/train_scanner_fastgs.py:957-960)
+        self.loss_mode = "l1_dssim"
         self.betas, self.eps, self.bias_correction = betas, float(eps), bool(bias_correction)
         self.pg = process_group
         flat = np.concatenate([scene.means3d.reshape(-1), scene.features_dc.reshape(-1),
@@ -500,8 +503,12 @@ class Trainer:
         dimg = ws.get("dimg", 3 * P, torch.float32)
         lscr = ws.get("loss_scr", int(L.fgs_loss_scratch_bytes(W, H)) // 4 + 1, torch.float32)
         lout = loss_out if loss_out is not None else ws.get("loss_out", 4, torch.float32)
-        self._call("loss", L.fgs_l1_dssim_loss, W, H, _p(img), _p(target), self.w_l1 * loss_scale,
-                                  self.w_ssim * loss_scale, _p(lout), _p(dimg), _p(lscr), st)
+        if self.loss_mode == "mse":
+            self._call("loss", L.fgs_mse_loss, W, H, _p(img), _p(target), loss_scale, _p(lout),
+                       _p(dimg), _p(lscr), st)
+        else:
+            self._call("loss", L.fgs_l1_dssim_loss, W, H, _p(img), _p(target), self.w_l1 * loss_scale,
+                       self.w_ssim * loss_scale, _p(lout), _p(dimg), _p(lscr), st)
         # backward
         # one zeroed buffer, each part starting on a 16-byte boundary (the
         # kernels read the conic and viewspace gradients as float4)

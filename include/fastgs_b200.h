@@ -405,6 +405,13 @@ FGS_API int fgs_l1_dssim_loss(int32_t width, int32_t height, const float* image,
                               const float* target, float w_l1, float w_ssim, float* loss_out,
                               float* dL_dimage, void* scratch, void* stream);
 
+/* loss = w_mse * mean (image - target)^2 over CHW [3,H,W] images, and
+ * dL/dimage: the reference trainer's loss before --mse-until
+ * (scripts/train_scanner_fastgs.py:824, 957-960). loss_out receives {loss,
+ * mean squared error, 0}; `scratch` holds fgs_loss_scratch_bytes(W, H) bytes. */
+FGS_API int fgs_mse_loss(int32_t width, int32_t height, const float* image, const float* target,
+                         float w_mse, float* loss_out, float* dL_dimage, void* scratch, void* stream);
+
 /* Adam over a flat buffer split into num_groups (<= 8) contiguous groups:
  * elements [group_end[k-1], group_end[k]) use group_lr[k] (host arrays).
  * m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2; p -= lr m' / (sqrt(v') + eps),

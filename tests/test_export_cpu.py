@@ -44,3 +44,53 @@ def test_spz_frame_change():
     want = E._AXIS @ E.quat_to_matrix(scene.rotations) @ E._AXIS.T
     np.testing.assert_allclose(rm, want, atol=3e-5)
     assert np.array_equal(a["scales"], scene.log_scales.reshape(-1))
+
+
+def test_spz_known_bytes(tmp_path):
+    """One hand-encoded point against the packed layout byte for byte."""
+    import gzip
+    import struct
+
+    cloud = {"positions": np.array([1.0, -2.5, 0.000244140625], np.float32),
+             "alphas": np.array([0.0], np.float32), "colors": np.array([0.0, 1.0, -1.0], np.float32),
+             "scales": np.array([-4.0, -10.0, 6.0], np.float32),
+             "rotations": np.array([0.0, 0.0, 0.0, -1.0], np.float32),  # x y z w; w < 0 flips
+             "sh": np.array([0.5, -0.25, 0.0] * 3 + [1.0, -1.0, 0.1] * 5, np.float32)}
+    p = tmp_path / "one.spz"
+    E.write_spz(p, cloud, 2)
+    raw = gzip.open(p, "rb").read()
+    assert struct.unpack_from("<IIIBBBB", raw) == (0x5053474E, 2, 1, 2, 12, 1, 0)
+    body = raw[16:]
+    pos = body[:9]
+    assert pos == bytes([0x00, 0x10, 0x00, 0x00, 0xD8, 0xFF, 0x01, 0x00, 0x00])  # 4096, -10240, 1
+    assert body[9] == 128                                  # sigmoid(0) * 255 = 127.5 -> 128
+    assert list(body[10:13]) == [128, 166, 89]             # 127.5 + c * 38.25, rounded
+    assert list(body[13:16]) == [96, 0, 255]               # (s + 10) * 16, clamped
+    assert list(body[16:19]) == [128, 128, 128]            # (0, 0, 0, 1) after the sign flip
+    # degree 1 (9 values, buckets of 8), then 15 values in buckets of 16
+    assert list(body[19:28]) == [192, 96, 128] * 3
+    assert list(body[28:43]) == [255, 0, 144] * 5
+    assert len(body) == 43
+
+
+def test_spz_round_trip(tmp_path):
+    scene, _ = S.small_scene(5, 500, 3, 32, 32)
+    a = E.spz_cloud_arrays(_params(scene))
+    p = tmp_path / "scene.spz"
+    E.write_spz(p, a, 3)
+    b = E.read_spz(p)
+    assert b["sh_degree"] == 3 and b["antialiased"]
+    np.testing.assert_allclose(b["positions"], a["positions"], atol=0.5 / 4096 + 1e-7)
+    np.testing.assert_allclose(b["scales"], np.clip(a["scales"], -10, 255 / 16 - 10), atol=0.5 / 16 + 1e-6)
+    np.testing.assert_allclose(b["colors"], np.clip(a["colors"], -127.5 / 38.25, 127.5 / 38.25),
+                               atol=0.5 / 38.25 + 1e-6)
+    op_a = 1 / (1 + np.exp(-a["alphas"]))
+    op_b = 1 / (1 + np.exp(-b["alphas"].astype(np.float64)))
+    np.testing.assert_allclose(op_b, op_a, atol=0.5 / 255 + 1e-6)
+    qa = a["rotations"].reshape(-1, 4)
+    qa = qa / np.linalg.norm(qa, axis=1, keepdims=True) * np.where(qa[:, 3:4] < 0, -1, 1)
+    qb = b["rotations"].reshape(-1, 4)
+    assert np.abs(qb[:, :3] - qa[:, :3]).max() <= 0.5 / 127.5 + 1e-6
+    sh_a, sh_b = a["sh"].reshape(500, -1), b["sh"].reshape(500, -1)
+    assert np.abs(sh_b[:, :9] - np.clip(sh_a[:, :9], -1, 127 / 128)).max() <= 4.5 / 128
+    assert np.abs(sh_b[:, 9:] - np.clip(sh_a[:, 9:], -1, 127 / 128)).max() <= 8.5 / 128

@@ -315,3 +315,44 @@ def test_l1_dssim_loss_autograd(cuda_dev):
     ref.backward()
     assert abs(loss.item() - ref.item()) < 1e-5 * max(1.0, abs(ref.item()))
     assert rel_err(img.grad.cpu().numpy(), x.grad.cpu().numpy()) < 1e-4
+
+
+@pytest.mark.parametrize("W,H", [(64, 48), (1920, 1080)])
+def test_mse_loss(W, H, cuda_dev):
+    """fgs_mse_loss (the reference trainer's warm-up loss) against torch fp32."""
+    g = torch.Generator(device="cpu").manual_seed(W + 1)
+    img = torch.rand((3, H, W), generator=g).to(cuda_dev)
+    tgt = torch.rand((3, H, W), generator=g).to(cuda_dev)
+    L = _lib.lib()
+    scr = torch.empty(int(L.fgs_loss_scratch_bytes(W, H)) // 4 + 1, device=cuda_dev)
+    out = torch.empty(3, device=cuda_dev)
+    dimg = torch.empty_like(img)
+    _lib.check(L.fgs_mse_loss(W, H, _p(img), _p(tgt), 0.5, _p(out), _p(dimg), _p(scr), _stream()), "mse")
+    x = img.clone().requires_grad_(True)
+    ref = 0.5 * ((x - tgt) ** 2).mean()
+    ref.backward()
+    assert abs(out[0].item() - ref.item()) < 1e-5 * max(1.0, abs(ref.item()))
+    assert abs(out[1].item() - 2 * ref.item()) < 1e-5
+    assert rel_err(dimg.cpu().numpy(), x.grad.cpu().numpy()) < 1e-5
+
+
+def test_driver_mse_warmup(cuda_dev):
+    """FastGSDriver uses the MSE loss up to mse_until and L1 (+ D-SSIM) after."""
+    from fastgs_core_b200.policy import DriverConfig, FastGSDriver
+
+    scene, cam = S.small_scene(13, 1500, 3, 64, 48)
+    target = torch.rand(3 * 64 * 48, generator=torch.Generator().manual_seed(2)).to(cuda_dev)
+    tr = Trainer(scene, cuda_dev, w_ssim=0.0)
+    drv = FastGSDriver(tr, [cam], [target], DriverConfig(mse_until=2, densify_until_step=0,
+                                                         final_prune_start=10**9), seed=3)
+    lo = torch.zeros(4, device=cuda_dev)
+    modes = []
+    for _ in range(4):
+        drv.step(loss_out=lo)
+        torch.cuda.synchronize()
+        modes.append(tr.loss_mode)
+        img = tr.ws.b["img"][:3 * 64 * 48]
+        d = img - target
+        want = (d * d).mean() if tr.loss_mode == "mse" else d.abs().mean()
+        assert abs(lo[0].item() - want.item()) < 1e-4
+    assert modes == ["mse", "mse", "l1_dssim", "l1_dssim"]
