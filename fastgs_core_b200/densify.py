@@ -18,9 +18,12 @@ never split (the split masks are padded with False), and the pruning scores
 follow their rows through the clone, split and prune steps (appended rows
 score 0).
 
-Functions take the Trainer (fastgs_core_b200.train.Trainer, one rank) and
-numpy arrays for host-side scores; they return the reference's statistics
-dicts.
+Functions take the Trainer (fastgs_core_b200.train.Trainer) and numpy
+arrays for host-side scores; they return the reference's statistics dicts.
+Under view-sharded data parallelism every rank calls them in the same order
+with an equally seeded generator: decisions use the all-reduced statistics
+and rank 0's scores, parameters are replicated, and the Adam moments are
+all-gathered for the row gathers and re-sharded by Trainer._resize.
 """
 from __future__ import annotations
 
@@ -78,8 +81,9 @@ def _apply_rows(tr, param_index: np.ndarray, moment_index: np.ndarray, keep_stat
     mi = torch.from_numpy(moment_index.astype(np.int64)).to(dev)
     size = _padded(n_out)
     params = _gather(tr.params_pad, n_in, n_out, pi, PARAM_WIDTHS, size)
-    m = _gather(tr.exp_avg, n_in, n_out, mi, PARAM_WIDTHS, size)
-    v = _gather(tr.exp_avg_sq, n_in, n_out, mi, PARAM_WIDTHS, size)
+    m_full, v_full = tr.full_moments()  # all-gathered when sharded over ranks
+    m = _gather(m_full, n_in, n_out, mi, PARAM_WIDTHS, size)
+    v = _gather(v_full, n_in, n_out, mi, PARAM_WIDTHS, size)
     if keep_stats:
         stats = _gather(tr.stats, n_in, n_out, pi, STATS_WIDTHS, 4 * n_out)
     else:
@@ -146,10 +150,18 @@ def densify_and_split(tr, metric_mask, split_filter, rng, split_factor: int, sco
 
 def cap_opacity_logits(tr, opacity_cap: float):
     """cap_opacity_logits (:621-638): logit(min(opacity, cap)); the opacity
-    moments restart at zero."""
-    check(lib().fgs_opacity_cap(tr.n, float(opacity_cap), _p(tr.params_pad), _p(tr.exp_avg),
-                                _p(tr.exp_avg_sq), torch.cuda.current_stream(tr.dev).cuda_stream),
-          "opacity_cap")
+    moments restart at zero (with sharded moments: this rank's part of the
+    opacity segment)."""
+    sharded = tr.world > 1
+    check(lib().fgs_opacity_cap(tr.n, float(opacity_cap), _p(tr.params_pad),
+                                None if sharded else _p(tr.exp_avg),
+                                None if sharded else _p(tr.exp_avg_sq),
+                                torch.cuda.current_stream(tr.dev).cuda_stream), "opacity_cap")
+    if sharded:
+        a, b = max(51 * tr.n, tr._lo), min(52 * tr.n, tr._hi)
+        if a < b:
+            tr.exp_avg[a - tr._lo:b - tr._lo].zero_()
+            tr.exp_avg_sq[a - tr._lo:b - tr._lo].zero_()
 
 
 def reset_opacity_logits(tr, reset_value: float):
@@ -166,10 +178,13 @@ def _masks(tr, fn_name, *args) -> np.ndarray:
 
 def densify_and_prune_fastgs(tr, args: DensifyArgs, scene_extent: float, importance_score,
                              pruning_score, rng) -> dict:
-    """densify_and_prune_fastgs (:661-745) on the trainer's running
-    statistics (tr.stats)."""
+    """densify_and_prune_fastgs (:661-745) on the running statistics of
+    every rank's views (tr.global_stats(); the trainer's own with one rank).
+    With several ranks every rank calls it with the same scores and an
+    equally seeded generator, so all make the same choices."""
     imp = torch.as_tensor(np.asarray(importance_score, np.float32), device=tr.dev)
-    mk = _masks(tr, "fgs_densify_masks", _p(tr.params_pad), _p(tr.stats), _p(imp),
+    gstats = tr.global_stats() if tr.world > 1 else tr.stats
+    mk = _masks(tr, "fgs_densify_masks", _p(tr.params_pad), _p(gstats), _p(imp),
                 float(args.grad_thresh), float(args.grad_abs_thresh),
                 float(args.dense * scene_extent), float(args.importance_score_threshold))
     clone_sel = (mk & 1) != 0
@@ -180,7 +195,8 @@ def densify_and_prune_fastgs(tr, args: DensifyArgs, scene_extent: float, importa
     split_sources, split_children, score = densify_and_split(tr, metric, split_sel, rng,
                                                              int(args.split_factor), score)
     n = tr.n
-    pm = _masks(tr, "fgs_prune_masks", _p(tr.params_pad), _p(tr.stats[3 * n:]),
+    gstats = tr.global_stats() if tr.world > 1 else tr.stats
+    pm = _masks(tr, "fgs_prune_masks", _p(tr.params_pad), _p(gstats[3 * n:]),
                 float(args.min_opacity), float(args.max_screen_size),
                 float(args.max_world_scale_factor * scene_extent if args.max_world_scale_factor > 0 else 0.0))
     opacity_prune = (pm & 1) != 0
@@ -249,6 +265,13 @@ def compute_gaussian_scores_fastgs(tr, cams, targets, camera_indices, loss_thres
     fin = torch.empty(2, dtype=torch.int32, device=dev)
     check(L.fgs_score_finalize(n, _p(counts), _p(score), len(idx), _p(imp) if densify else None,
                                _p(pruning), _p(fin), st), "score_finalize")
+    if tr.world > 1:
+        # every rank rendered the same views; the float sums may still differ
+        # in their last bits between ranks, so all use rank 0's scores
+        import torch.distributed as dist
+
+        dist.broadcast(imp, 0, group=tr.pg)
+        dist.broadcast(pruning, 0, group=tr.pg)
     return (imp.cpu().numpy() if densify else None), pruning.cpu().numpy()
 
 

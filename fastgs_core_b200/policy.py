@@ -147,7 +147,10 @@ def sample_camera_indices(rng, num_cameras: int, sample_count: int) -> np.ndarra
 
 class FastGSDriver:
     """Steps a Trainer through the reference's schedule. cameras: the
-    training views; targets: their [3, H*W] float32 device images."""
+    training views; targets: their [3, H*W] float32 device images. With a
+    data-parallel Trainer every rank runs its own driver with the same seed:
+    each step renders one view per rank, and the densification and pruning
+    decisions are the same on every rank."""
 
     def __init__(self, trainer: Trainer, cameras, targets, cfg: DriverConfig | None = None,
                  policy: OptimizerPolicy | None = None, seed: int = 42,
@@ -190,10 +193,15 @@ class FastGSDriver:
             self.active_sh_degree = min(self.active_sh_degree + 1, c.sh_degree)
         tr.sh_degree = self.active_sh_degree
         tr.loss_mode = "l1_dssim" if step > c.mse_until else "mse"
-        if not self.viewpoint_stack:
-            self.viewpoint_stack = list(range(len(self.cameras)))
-        idx = self.viewpoint_stack.pop(int(self.rng.integers(0, len(self.viewpoint_stack))))
-        tr.step([self.cameras[idx]], [self.targets[idx]], loss_out=loss_out)
+        # one view per rank and step, drawn without replacement (every rank
+        # draws the same ones from its equally seeded generator)
+        views = []
+        for _ in range(tr.world):
+            if not self.viewpoint_stack:
+                self.viewpoint_stack = list(range(len(self.cameras)))
+            views.append(self.viewpoint_stack.pop(int(self.rng.integers(0, len(self.viewpoint_stack)))))
+        tr.step([self.cameras[i] for i in views], [self.targets[i] for i in views], loss_out=loss_out)
+        idx = views[0] if len(views) == 1 else views
         out = {"step": step, "view": idx, "sh_degree": self.active_sh_degree, "points": tr.n}
         if step < c.densify_until_step:
             if step > c.densify_from_step and step % c.densification_interval == 0:

@@ -243,31 +243,65 @@ class Trainer:
         self.events: dict[str, list] = {}
         self.launches = 0
 
+    def full_moments(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Adam moments of every flat element (59 n floats each): this rank's
+        shards, all-gathered when the moments are sharded over ranks."""
+        total = FLOATS_PER_GAUSSIAN * self.n
+        if self.world == 1:
+            return self.exp_avg[:total], self.exp_avg_sq[:total]
+        import torch.distributed as dist
+
+        out = []
+        for t in (self.exp_avg, self.exp_avg_sq):
+            full = torch.empty(self._per * self.world, device=self.dev)
+            dist.all_gather_into_tensor(full, t.contiguous(), group=self.pg)
+            out.append(full[:total])
+        return out[0], out[1]
+
     def _resize(self, n_new: int, params_new: torch.Tensor, exp_avg_new: torch.Tensor,
                 exp_avg_sq_new: torch.Tensor, stats_new: torch.Tensor) -> None:
         """Adopt buffers for n_new Gaussians (densification): the flat
-        parameters and moments (padded to the layout's shard size), the
-        running statistics [acc | acc_abs | denom | max_radii]; gradients and
-        per-step statistics restart at zero."""
-        if self.world > 1:
-            raise NotImplementedError("densification runs on one rank (world size 1)")
+        parameters and the full (unsharded) moments, at least 59 n_new floats
+        each, and this rank's running statistics [acc | acc_abs | denom |
+        max_radii]; gradients and per-step statistics restart at zero. With
+        several ranks every rank calls it with the same parameters and
+        moments (the decisions are made on global statistics with one
+        generator): each keeps its shard of the moments, and the symmetric
+        parameter and gradient buffers are allocated and registered anew."""
         d = self.dev
         total = FLOATS_PER_GAUSSIAN * n_new
         self.n = n_new
-        self._per = -(-total // 4) * 4
-        self.params_pad, self.exp_avg, self.exp_avg_sq = params_new, exp_avg_new, exp_avg_sq_new
-        assert params_new.numel() == self._per and exp_avg_new.numel() == self._per
-        self.grads_pad = torch.zeros(self._per, device=d)
+        self._per = -(-total // (4 * self.world)) * 4
+        padded = self._per * self.world
+        self._symm = None
+        if self.comm == "multicast":
+            self._symm = _symmetric_pair(padded, d, self.pg)
+            if self._symm is None:
+                self.comm = "nccl"
+        if self._symm is not None:
+            self.params_pad, self.grads_pad, self._hp, self._hg = self._symm
+        else:
+            self.params_pad = torch.empty(padded, device=d)
+            self.grads_pad = torch.empty(padded, device=d)
+        self.params_pad.zero_()
+        self.grads_pad.zero_()
+        self.params_pad[:total].copy_(params_new[:total])
         self.params = self.params_pad[:total]
         self.grads = self.grads_pad[:total]
-        self._lo, self._hi = 0, total
+        self._lo, self._hi = shard_range(total, self.world, self.rank)
+        self.exp_avg = torch.zeros(self._per, device=d)
+        self.exp_avg_sq = torch.zeros(self._per, device=d)
+        self.exp_avg[:self._hi - self._lo].copy_(exp_avg_new[self._lo:self._hi])
+        self.exp_avg_sq[:self._hi - self._lo].copy_(exp_avg_sq_new[self._lo:self._hi])
         self.stats = stats_new
         self.step_stats = torch.zeros((STATS_SUM + 1) * n_new, device=d)
         self.opacities = torch.empty(n_new, device=d)
         self.scales = torch.empty((n_new, 3), device=d)
         self.quats = torch.empty((n_new, 4), device=d)
-        ends = np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n_new
+        ends = np.clip(np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n_new - self._lo, 0,
+                       self._hi - self._lo)
         self._group_end = (C.c_int64 * 6)(*ends.tolist())
+        self._vs_zeroed = False
 
     # kernels each C entry point launches (memsets are not kernels)
     _KERNELS = {"preprocess": 1, "depth_order": 8, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
