@@ -153,12 +153,17 @@ def _run_preprocess_backward(prm: PreprocessParams, t: dict, fwd: dict, cot: dic
         v = cot.get(k)
         return z(*shape) if v is None else _f32(v, dev)
 
+    # the cotangents are bound to names for the whole call: a raw pointer into
+    # a temporary would dangle once the temporary is freed, and the caching
+    # allocator would hand its memory to the next temporary
     dcov = cot.get("cov3d")
+    dcov = None if dcov is None else _f32(dcov, dev)
+    drgb, dxys = c("rgb", n, 3), c("xys", n, 2)
+    dconic, dvs = c("conic_opacity", n, 4), c("viewspace_points", n, 4)
     st = lib().fgs_preprocess_backward(
         C.byref(prm), *[_p(t[k]) for k in ("means3d", "scales", "quats", "viewmat", "projmat",
                                            "cam_pos", "sh", "cov3d_precomp")],
-        _p(fwd["cov3d"]), _p(None if dcov is None else _f32(dcov, dev)), _p(c("rgb", n, 3)),
-        _p(c("xys", n, 2)), _p(c("conic_opacity", n, 4)), _p(c("viewspace_points", n, 4)),
+        _p(fwd["cov3d"]), _p(dcov), _p(drgb), _p(dxys), _p(dconic), _p(dvs),
         _p(fwd["radii"]), _p(fwd["clamped"]),
         *[_p(g[k]) for k in ("dmeans3d", "ddc", "dsh", "dcolors_precomp", "dopacities", "dscales",
                              "dquats", "dviewspace")], _stream(dev))
@@ -329,13 +334,17 @@ def binning_forward(xys, depths, point_offsets, conic_opacity, tiles_touched, mu
     keys = torch.empty(num_rendered, dtype=torch.uint64, device=dev)
     vals = torch.empty(num_rendered, dtype=torch.uint32, device=dev)
     if num_rendered > 0:
+        # converted inputs stay bound to names until the call returns (a raw
+        # pointer into a freed temporary could be handed to the next one)
         xys = _f32(xys, dev)
+        depths = _f32(depths, dev)
+        offs = _int_t(point_offsets, torch.uint32, dev)
+        conic = _f32(conic_opacity, dev)
+        tiles = _int_t(tiles_touched, torch.uint32, dev)
         n = xys.shape[0]
         check(lib().fgs_duplicate_with_keys(
-            n, float(mult), int(tile_bounds_x), int(tile_bounds_y), _p(xys),
-            _p(_f32(depths, dev)), _p(_int_t(point_offsets, torch.uint32, dev)),
-            _p(_f32(conic_opacity, dev)), _p(_int_t(tiles_touched, torch.uint32, dev)),
-            num_rendered, _p(keys), _p(vals), _stream(dev)), "binning_forward")
+            n, float(mult), int(tile_bounds_x), int(tile_bounds_y), _p(xys), _p(depths), _p(offs),
+            _p(conic), _p(tiles), num_rendered, _p(keys), _p(vals), _stream(dev)), "binning_forward")
     return {"point_list_keys_unsorted": keys, "point_list_unsorted": vals}
 
 
@@ -355,8 +364,9 @@ def sort_keys(keys: torch.Tensor, values: torch.Tensor, num_tiles: int | None = 
     if k:
         nbytes = int(lib().fgs_sort_workspace_bytes(k, key_bits))
         ws = _WS.get(dev, "sort", nbytes)
-        check(lib().fgs_sort_pairs(k, int(key_bits), _p(keys.contiguous()), _p(values.contiguous()),
-                                   _p(ko), _p(vo), _p(ws), ws.numel(), _stream(dev)), "sort_keys")
+        kin, vin = keys.contiguous(), values.contiguous()  # alive for the whole call
+        check(lib().fgs_sort_pairs(k, int(key_bits), _p(kin), _p(vin), _p(ko), _p(vo), _p(ws),
+                                   ws.numel(), _stream(dev)), "sort_keys")
         if check_status:
             sort_status(dev)
     return ko, vo

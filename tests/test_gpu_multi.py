@@ -70,7 +70,8 @@ def _run(tr, cams, targets, mode):
     for _ in range(2):
         tr.step(cams, targets)
     imp, pruning = _densify_inputs(tr.n)
-    res = D.densify_and_prune_fastgs(tr, _densify_args(), 2.0, imp, pruning, np.random.default_rng(9))
+    # scene extent 5: dense bound 0.05 sits inside the log-scale spread (clones and splits)
+    res = D.densify_and_prune_fastgs(tr, _densify_args(), 5.0, imp, pruning, np.random.default_rng(9))
     tr.step(cams, targets)
     return res
 
