@@ -352,6 +352,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--n", type=int, default=1_000_000, help="Gaussians (default: config 3)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-api", action="store_true",
+                    help="skip the e2e_api leg (profiling runs that capture the step's launches)")
     ap.add_argument("--config", type=int, default=3, choices=[3, 4, 5])
     args = ap.parse_args()
     if args.impl == "reference":
@@ -536,7 +538,7 @@ def main():
                     "d2h_bytes_per_step": 16},
             "clocks": clk,
         }
-        if world == 1:
+        if world == 1 and not args.no_api:
             # the reference's own call sequence through the drop-in API
             api_v, api_ms = api_e2e(scene, cams, host_targets, min(args.steps, 100), warmup, dev)
             line["e2e_api"] = {"value": api_v, "unit": "views/s", "ms_per_step": api_ms,
