@@ -179,7 +179,17 @@ __global__ void __launch_bounds__(kSortThreads)
 #pragma unroll
   for (int i = 0; i < kSortItems; ++i) {
     const uint32_t d = (uint32_t)(k[i] >> shift) & 0xffu;
+#ifdef FGS_SORT_MATCH_ANY
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
+#else
+    // the lanes holding the same digit: one ballot per digit bit
+    uint32_t peers = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (d >> b) & 1u);
+      peers &= ((d >> b) & 1u) ? bal : ~bal;
+    }
+#endif
     const uint32_t before = s_whist[w][d];
     __syncwarp();
     if (lane == (__ffs(peers) - 1)) s_whist[w][d] = before + __popc(peers);
