@@ -437,6 +437,60 @@ __device__ __forceinline__ void adam4(float4& pp, float4& mm, float4& vv, const 
   }
 }
 
+// ---------------------------------------- Adam fused with a unicast exchange
+// Data-parallel update over plain peer loads and stores: the owner of a shard
+// sums every rank's gradient for it (ranks in order; its own from local
+// memory, the others' over NVLink), applies Adam to its shard and stores the
+// new parameters into every rank's copy. Per GPU this moves (world - 1) /
+// world of the buffer in each direction twice (gradients in, parameters
+// out), which at two ranks is less than the multicast kernel's traffic.
+constexpr int kMaxPeers = 8;
+struct PeerPtrs {
+  float* p[kMaxPeers];
+  const float* g[kMaxPeers];
+};
+constexpr int kPeerUnroll = 2;
+
+__global__ void __launch_bounds__(256)
+    adam_peers_kernel(int64_t n4, int world, int rank, PeerPtrs pp, float* __restrict__ m,
+                      float* __restrict__ v, AdamGroups grp, float b1, float b2, float eps,
+                      float bc1, float bc2) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t base = t; base < n4; base += stride * kPeerUnroll) {
+    float4 gg[kPeerUnroll];
+#pragma unroll
+    for (int u = 0; u < kPeerUnroll; ++u) {
+      const int64_t i4 = base + u * stride;
+      if (i4 >= n4) continue;
+      // peers' memory is read past L1 (it changes every step)
+      float4 a = __ldcg(reinterpret_cast<const float4*>(pp.g[0]) + i4);
+      for (int r = 1; r < world; ++r) {
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(pp.g[r]) + i4);
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+      }
+      gg[u] = a;
+    }
+#pragma unroll
+    for (int u = 0; u < kPeerUnroll; ++u) {
+      const int64_t i4 = base + u * stride;
+      if (i4 >= n4) break;
+      float4 p4 = reinterpret_cast<const float4*>(pp.p[rank])[i4];
+      float4 mm = reinterpret_cast<float4*>(m)[i4];
+      float4 vv = reinterpret_cast<float4*>(v)[i4];
+      adam4(p4, mm, vv, gg[u], 4 * i4, grp, b1, b2, eps, bc1, bc2);
+      reinterpret_cast<float4*>(m)[i4] = mm;
+      reinterpret_cast<float4*>(v)[i4] = vv;
+      for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(pp.p[r])[i4] = p4;
+    }
+  }
+  // make the stores to the peers visible system-wide before the caller's barrier
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 constexpr int kMcUnroll = 4;  // independent multicast loads in flight per thread
 
 __global__ void __launch_bounds__(256)
@@ -659,6 +713,53 @@ int fgs_adam_step(int64_t total, float* params, const float* grads, float* exp_a
   adam_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, (cudaStream_t)stream>>>(
       total, params, grads, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
   return check_launch("adam_step");
+}
+
+int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, float* const* params_ranks,
+                        const float* const* grads_ranks, float* exp_avg, float* exp_avg_sq,
+                        int32_t num_groups, const int64_t* group_end, const float* group_lr,
+                        float beta1, float beta2, float eps, int32_t step, int32_t bias_correction,
+                        void* stream) {
+  FGS_CHECK_ARG(shard >= 0 && shard % 4 == 0, "shard length must be a multiple of 4");
+  FGS_CHECK_ARG(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world,
+                "world must be in [1, %d] and rank in [0, world)", kMaxPeers);
+  FGS_CHECK_ARG(num_groups >= 1 && num_groups <= 8, "num_groups must be in [1, 8]");
+  FGS_CHECK_ARG(group_end && group_lr && params_ranks && grads_ranks, "missing pointer table");
+  if (shard == 0) return FGS_OK;
+  FGS_CHECK_ARG(exp_avg && exp_avg_sq, "missing pointer");
+  PeerPtrs pp;
+  memset(&pp, 0, sizeof(pp));
+  uintptr_t align = (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq;
+  for (int r = 0; r < world; ++r) {
+    FGS_CHECK_ARG(params_ranks[r] && grads_ranks[r], "missing pointer for rank %d", r);
+    pp.p[r] = params_ranks[r];
+    pp.g[r] = grads_ranks[r];
+    align |= (uintptr_t)params_ranks[r] | (uintptr_t)grads_ranks[r];
+  }
+  FGS_CHECK_ARG(align % 16 == 0, "buffers must be 16-byte aligned");
+  AdamGroups g;
+  memset(&g, 0, sizeof(g));
+  g.count = num_groups;
+  for (int k = 0; k < num_groups; ++k) {
+    g.end[k] = group_end[k];
+    g.lr[k] = group_lr[k];
+  }
+  float bc1 = 1.f, bc2 = 1.f;
+  if (bias_correction) {
+    FGS_CHECK_ARG(step >= 1, "step must be >= 1 with bias correction");
+    bc1 = 1.0f / (1.0f - powf(beta1, (float)step));
+    bc2 = 1.0f / (1.0f - powf(beta2, (float)step));
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n4 = shard / 4;
+  const int64_t want = (n4 + 255) / 256;
+  const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  adam_peers_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(n4, world, rank, pp, exp_avg,
+                                                              exp_avg_sq, g, beta1, beta2, eps,
+                                                              bc1, bc2);
+  return check_launch("adam_step_peers");
 }
 
 int fgs_adam_step_multicast(int64_t shard, const float* params_local, float* params_mc,

@@ -67,9 +67,10 @@ class _Grow:
         return t[:numel]
 
 
-def _symmetric_pair(numel: int, dev, group):
-    """Parameter and gradient buffers in symmetric memory bound to an NVLink
-    multicast object (None where that is unavailable)."""
+def _symmetric_pair(numel: int, dev, group, multicast: bool = True):
+    """Parameter and gradient buffers in symmetric memory, mapped on every
+    rank (peer pointers) and, with `multicast`, bound to an NVLink multicast
+    object (None where that is unavailable)."""
     try:
         import torch.distributed._symmetric_memory as symm
     except ImportError:
@@ -82,11 +83,27 @@ def _symmetric_pair(numel: int, dev, group):
         g = symm.empty(numel, dtype=torch.float32, device=dev)
         hp = symm.rendezvous(p, name)
         hg = symm.rendezvous(g, name)
-        if not getattr(hp, "multicast_ptr", 0) or not getattr(hg, "multicast_ptr", 0):
+        if multicast and (not getattr(hp, "multicast_ptr", 0) or not getattr(hg, "multicast_ptr", 0)):
+            return None
+        if not multicast and len(getattr(hp, "buffer_ptrs", ())) != dist_world(group):
             return None
         return p, g, hp, hg
     except Exception:
         return None
+
+
+def dist_world(group) -> int:
+    import torch.distributed as dist
+
+    return dist.get_world_size(group)
+
+
+def default_comm(world: int) -> str:
+    """The exchange a data-parallel step uses by default: at two ranks plain
+    peer loads and stores (fgs_adam_step_peers: 118 MB per direction and
+    phase at 1M Gaussians), beyond that the NVLink multicast kernel, whose
+    per-GPU traffic does not grow with the number of ranks."""
+    return "p2p" if world == 2 else "multicast"
 
 
 def local_views(num_views: int, world: int, rank: int) -> list[int]:
@@ -176,9 +193,9 @@ class Trainer:
         self.comm = "local"
         self._symm = None
         if self.world > 1:
-            self.comm = comm or os.environ.get("FGS_COMM", "") or "multicast"
-            if self.comm == "multicast":
-                self._symm = _symmetric_pair(padded, d, process_group)
+            self.comm = comm or os.environ.get("FGS_COMM", "") or default_comm(self.world)
+            if self.comm in ("multicast", "p2p"):
+                self._symm = _symmetric_pair(padded, d, process_group, self.comm == "multicast")
                 if self._symm is None:
                     self.comm = "nccl"
         if self._symm is not None:
@@ -274,8 +291,8 @@ class Trainer:
         self._per = -(-total // (4 * self.world)) * 4
         padded = self._per * self.world
         self._symm = None
-        if self.comm == "multicast":
-            self._symm = _symmetric_pair(padded, d, self.pg)
+        if self.comm in ("multicast", "p2p"):
+            self._symm = _symmetric_pair(padded, d, self.pg, self.comm == "multicast")
             if self._symm is None:
                 self.comm = "nccl"
         if self._symm is not None:
@@ -633,17 +650,25 @@ class Trainer:
         lr = self.lrs
         lrs = (C.c_float * 6)(lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations)
         b1, b2 = float(self.betas[0]), float(self.betas[1])
-        if self.comm == "multicast":
+        if self.comm in ("multicast", "p2p"):
             # every rank's gradients written -> fused exchange + Adam -> every
             # rank's parameter broadcast landed (also guards the next step's
             # gradient writes against peers still reading these)
             ev = self._begin("exchange")
             self._hp.barrier(channel=0)
             off = lo * 4
-            self._call("adam", lib().fgs_adam_step_multicast, self._per, _p(self.params_pad[lo:]),
-                       C.c_void_p(self._hp.multicast_ptr + off), C.c_void_p(self._hg.multicast_ptr + off),
-                       _p(self.exp_avg), _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2,
-                       self.eps, self.step_count, int(self.bias_correction), self._stream())
+            if self.comm == "multicast":
+                self._call("adam", lib().fgs_adam_step_multicast, self._per, _p(self.params_pad[lo:]),
+                           C.c_void_p(self._hp.multicast_ptr + off),
+                           C.c_void_p(self._hg.multicast_ptr + off), _p(self.exp_avg),
+                           _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2, self.eps,
+                           self.step_count, int(self.bias_correction), self._stream())
+            else:
+                pp = (C.c_void_p * world)(*[self._hp.buffer_ptrs[r] + off for r in range(world)])
+                gp = (C.c_void_p * world)(*[self._hg.buffer_ptrs[r] + off for r in range(world)])
+                self._call("adam", lib().fgs_adam_step_peers, self._per, world, rank, pp, gp,
+                           _p(self.exp_avg), _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2,
+                           self.eps, self.step_count, int(self.bias_correction), self._stream())
             self._hp.barrier(channel=1)
             self._end("exchange", ev)
             return len(mine)

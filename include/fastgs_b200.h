@@ -439,6 +439,22 @@ FGS_API int fgs_adam_step_multicast(int64_t shard, const float* params_local, fl
                                     const float* group_lr, float beta1, float beta2, float eps,
                                     int32_t step, int32_t bias_correction, void* stream);
 
+/* Data-parallel Adam over plain peer loads and stores (new here; used at two
+ * ranks, where it moves less over NVLink than fgs_adam_step_multicast).
+ * params_ranks[r] / grads_ranks[r] (host arrays of `world` pointers) address
+ * rank r's copy of this rank's shard in this process (symmetric memory or
+ * peer mappings; r == rank is local). The kernel sums the ranks' gradients in
+ * rank order, applies the Adam rule of fgs_adam_step to the shard (moments
+ * exp_avg / exp_avg_sq are this rank's) and stores the new parameters into
+ * every rank's copy. Callers bracket it with a cross-rank barrier before (all
+ * gradients written) and after (all stores visible). Group ends are relative
+ * to the shard; world <= 8. */
+FGS_API int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, float* const* params_ranks,
+                                const float* const* grads_ranks, float* exp_avg, float* exp_avg_sq,
+                                int32_t num_groups, const int64_t* group_end,
+                                const float* group_lr, float beta1, float beta2, float eps,
+                                int32_t step, int32_t bias_correction, void* stream);
+
 /* FastGS multi-view score pass (scripts/train_scanner_fastgs.py:262-340):
  * fgs_metric_map: per-pixel mean |pred - target| over channels, min-max
  *   normalised, > loss_thresh -> metric_map [P] int32; *l1_sum (device) gets

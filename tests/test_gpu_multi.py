@@ -1,9 +1,9 @@
 """Data-parallel training on 2 GPUs (skipped with fewer), against one process
 that renders both views itself:
 
-* one step at the real Adam epsilon (1e-8), both exchanges (the NVLink
-  multicast kernel fgs_adam_step_multicast and NCCL reduce-scatter /
-  all-gather): the Adam moments agree within the float-atomic noise of the
+* one step at the real Adam epsilon (1e-8), every exchange (the NVLink
+  multicast kernel fgs_adam_step_multicast, the peer kernel
+  fgs_adam_step_peers, and NCCL reduce-scatter / all-gather): the Adam moments agree within the float-atomic noise of the
   gradients; the parameter update agrees where the gradient stands out of
   that noise (elsewhere Adam's normalised step of a near-zero gradient takes
   either sign, and the test bounds it by the learning rate); the
@@ -143,13 +143,13 @@ def _rel(a, b):
     return float((a - b).abs().max() / max(float(b.abs().max()), 1e-30))
 
 
-@pytest.mark.parametrize("comm", ["multicast", "nccl"])
+@pytest.mark.parametrize("comm", ["multicast", "p2p", "nccl"])
 def test_two_rank_step_matches_single_process(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     res = _spawn(comm, "step", 1e-8)
-    if comm == "multicast" and res[0][1] != "multicast":
-        pytest.skip("NVLink multicast unavailable on this box")
+    if comm != "nccl" and res[0][1] != comm:
+        pytest.skip("symmetric memory (NVLink multicast / peer mappings) unavailable on this box")
     assert res[0][1] == comm
     tr, _, (_, n, want_p, want_m, want_v, want_s) = _single("step", 1e-8)
     g = tr.grads.cpu()
@@ -170,15 +170,15 @@ def test_two_rank_step_matches_single_process(comm):
     assert big.float().mean() > 0.3
 
 
-@pytest.mark.parametrize("comm", ["multicast", "nccl"])
+@pytest.mark.parametrize("comm", ["multicast", "p2p", "nccl"])
 def test_two_rank_densify_matches_single_process(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     # eps = 1: Adam's update is linear in the gradient, so the two runs' float
     # noise does not grow into different sign decisions over the steps
     res = _spawn(comm, "densify", 1.0)
-    if comm == "multicast" and res[0][1] != "multicast":
-        pytest.skip("NVLink multicast unavailable on this box")
+    if comm != "nccl" and res[0][1] != comm:
+        pytest.skip("symmetric memory (NVLink multicast / peer mappings) unavailable on this box")
     _, want_res, (_, n, want_p, want_m, want_v, want_s) = _single("densify", 1.0)
     assert want_res["cloned"] > 0 and want_res["split_sources"] > 0
     for r in range(2):
