@@ -169,6 +169,23 @@ class FastGSDriver:
         self.viewpoint_stack: list[int] = []
         self.log: list[dict] = []
 
+    def state_dict(self) -> dict:
+        """The Trainer's state plus the driver's: step, SH degree, view stack
+        and the generator's state (a resumed run draws the same views and
+        makes the same densification choices)."""
+        return {"trainer": self.tr.state_dict(), "step_index": self.step_index,
+                "active_sh_degree": self.active_sh_degree,
+                "viewpoint_stack": list(self.viewpoint_stack),
+                "rng": self.rng.bit_generator.state, "scene_extent": self.scene_extent}
+
+    def load_state_dict(self, state: dict) -> None:
+        self.tr.load_state_dict(state["trainer"])
+        self.step_index = int(state["step_index"])
+        self.active_sh_degree = int(state["active_sh_degree"])
+        self.viewpoint_stack = list(state["viewpoint_stack"])
+        self.rng.bit_generator.state = state["rng"]
+        self.scene_extent = float(state["scene_extent"])
+
     def _frozen(self, step: int) -> tuple:
         c = self.cfg
         frozen = []

@@ -259,6 +259,8 @@ class Trainer:
         self.fuse_adam = os.environ.get("FGS_FUSE_ADAM", "1") != "0"
         self.events: dict[str, list] = {}
         self.launches = 0
+        # NVTX ranges around every library call (FGS_NVTX=1), for timeline tools
+        self.nvtx = os.environ.get("FGS_NVTX", "0") == "1"
 
     def full_moments(self) -> tuple[torch.Tensor, torch.Tensor]:
         """Adam moments of every flat element (59 n floats each): this rank's
@@ -331,7 +333,11 @@ class Trainer:
         if name in self.record:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(name)
         check(fn(*args), name)
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
         if ev is not None:
             ev[1].record()
             self.events.setdefault(name, []).append(ev)
@@ -596,6 +602,38 @@ class Trainer:
             if int(f[0]) or int(f[1]):
                 raise RuntimeError(f"sort of view {v} failed (status {_lib.FGS_ERR_TIMEOUT}): a "
                                    "look-back wait gave up after its poll limit")
+
+    # -- checkpoint ---------------------------------------------------------
+    def state_dict(self) -> dict:
+        """Everything a resumed run needs, as CPU tensors: the raw parameters
+        [59 n], the full Adam moments (all-gathered when sharded), the running
+        densification statistics over every rank's views, the step count.
+        A collective with several ranks (every rank calls it; all get the
+        same dictionary)."""
+        m, v = self.full_moments()
+        return {"n": self.n, "step_count": self.step_count, "sh_degree": self.sh_degree,
+                "params": self.params.detach().cpu().clone(), "exp_avg": m.cpu().clone(),
+                "exp_avg_sq": v.cpu().clone(), "stats": self.global_stats().cpu(),
+                "betas": tuple(self.betas), "eps": self.eps,
+                "bias_correction": self.bias_correction}
+
+    def load_state_dict(self, state: dict) -> None:
+        """Resume from state_dict() (of this or another world size): every
+        rank adopts the parameters and its shard of the moments; the
+        statistics go to rank 0 (the others start at zero, so their sum and
+        maximum over ranks are the saved ones)."""
+        d = self.dev
+        n = int(state["n"])
+        total = FLOATS_PER_GAUSSIAN * n
+        params = state["params"].to(d, torch.float32).reshape(-1)[:total]
+        m = state["exp_avg"].to(d, torch.float32).reshape(-1)[:total]
+        v = state["exp_avg_sq"].to(d, torch.float32).reshape(-1)[:total]
+        stats = state["stats"].to(d, torch.float32).reshape(-1).clone()
+        if self.rank != 0:
+            stats.zero_()
+        self._resize(n, params, m, v, stats)
+        self.step_count = int(state["step_count"])
+        self.sh_degree = int(state.get("sh_degree", self.sh_degree))
 
     def check_sort_status(self) -> None:
         """Synchronise and raise if any sort since the last check timed out."""

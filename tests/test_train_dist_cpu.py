@@ -87,3 +87,45 @@ def test_sharded_update_matches_single_process(world):
         st = res[r][3]
         assert torch.allclose(st[: STATS_SUM * n], 1 + ssum, atol=1e-6)
         assert torch.equal(st[STATS_SUM * n:], torch.maximum(torch.ones(n), smax))
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 fails before the step's collective; rank 0 must get an error
+    from the process group (its timeout or the closed connection), not hang."""
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "raised"))
+        q.close()
+        q.join_thread()
+        os._exit(3)  # dies between steps, nothing in flight
+    grads = torch.zeros(8 * world)
+    try:
+        reduce_scatter_grads(grads, world, rank)
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error: " + type(e).__name__))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_lost_rank_surfaces_as_an_error():
+    import time
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == "raised" and procs[1].exitcode == 3
+    assert res[0].startswith("error"), res[0]
+    assert time.time() - t0 < 100
