@@ -143,7 +143,7 @@ __device__ __forceinline__ v3 sh_color(int deg, v3 dir_unnorm, const float* dcp,
 }
 
 template <bool kRaw>
-__global__ void __launch_bounds__(kPreThreads) preprocess_fwd_kernel(PreArgs a) {
+__global__ void __launch_bounds__(kPreThreads, 8) preprocess_fwd_kernel(PreArgs a) {
   extern __shared__ float s_sh[];
   const fgs_preprocess_params& p = a.p;
   const int base = blockIdx.x * kPreThreads;
