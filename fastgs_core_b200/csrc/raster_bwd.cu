@@ -127,6 +127,76 @@ __device__ __forceinline__ float warp_transpose_sum11(const float (&p)[kSlots], 
   return w;
 }
 
+__device__ __forceinline__ float2 pk2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 bc2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Per-pair partials of one splat for a thread's two pixels, which share a
+// column (one dx) and sit two rows apart (dy.x, dy.y), on the contribution-mask
+// path: v0 / v1 say whether the pair contributed in the forward pass. Pixel
+// state (T, the remaining-colour dot adot, dL/dpixel d0..d2, and -T_final
+// (bg . dL/dpixel) in ntfbg) is packed per pixel pair so that the arithmetic
+// issues as f32x2 instructions. The exponential is the fast one except close
+// to the 0.99 clamp, where the forward pass's exact arithmetic decides on
+// which side of the clamp the pair lies (only that side passes a gradient to
+// G). Writes the eleven slot sums of the two pixels into p.
+__device__ __forceinline__ void mask_pair_partials(float (&p)[kSlots], const float4 r0,
+                                                   const float4 r1, const float4 r2, bool v0,
+                                                   bool v1, float pfx, float2 npfy, float2& T,
+                                                   float2& adot, float2 d0, float2 d1, float2 d2,
+                                                   float2 ntfbg) {
+  const float dx = r0.x - pfx;
+  const float2 dy = __fadd2_rn(bc2(r0.y), npfy);
+  // power = -0.5 (a dx^2 + c dy^2) - b dx dy = -0.5 a dx^2 + dy (-0.5 c dy - b dx)
+  const float adx = r0.z * dx, bdx = r0.w * dx;
+  const float2 t = __ffma2_rn(bc2(-0.5f * r1.x), dy, bc2(-bdx));
+  const float2 power = __ffma2_rn(t, dy, bc2(-0.5f * adx * dx));
+  const float2 pl = __fmul2_rn(power, bc2(1.44269504f));
+  float2 G = pk2(ex2_approx(pl.x), ex2_approx(pl.y));
+  float2 oG = __fmul2_rn(bc2(r1.y), G);
+  if (v0 && fabsf(oG.x - 0.99f) < 1e-4f) {
+    G.x = fgs_expf_neg(splat_power(r0.z, r0.w, r1.x, dx, dy.x));
+    oG.x = __fmul_rn(r1.y, G.x);
+  }
+  if (v1 && fabsf(oG.y - 0.99f) < 1e-4f) {
+    G.y = fgs_expf_neg(splat_power(r0.z, r0.w, r1.x, dx, dy.y));
+    oG.y = __fmul_rn(r1.y, G.y);
+  }
+  const bool vg0 = v0 && !(oG.x > 0.99f), vg1 = v1 && !(oG.y > 0.99f);
+  const float2 al = pk2(v0 ? fmin_t(0.99f, oG.x) : 0.0f, v1 ? fmin_t(0.99f, oG.y) : 0.0f);
+  const float2 wgt = __fmul2_rn(al, T);
+  const float2 om = __ffma2_rn(al, bc2(-1.0f), bc2(1.0f));
+  const float2 rec = pk2(__fdividef(1.0f, om.x), __fdividef(1.0f, om.y));
+  const float2 cdot =
+      __ffma2_rn(bc2(r2.x), d2, __ffma2_rn(bc2(r1.w), d1, __fmul2_rn(bc2(r1.z), d0)));
+  adot = __ffma2_rn(wgt, cdot, adot);  // remaining colour after this splat, dotted with dL/dpix
+  const float2 dla = __ffma2_rn(T, cdot, __fmul2_rn(rec, __fadd2_rn(adot, ntfbg)));
+  T = __fmul2_rn(T, om);
+  const float2 cr = __fmul2_rn(wgt, d0), cg = __fmul2_rn(wgt, d1), cb = __fmul2_rn(wgt, d2);
+  p[kR] = cr.x + cr.y;
+  p[kG] = cg.x + cg.y;
+  p[kB] = cb.x + cb.y;
+  // dL/dG * G; the constant factors (-W/2, -H/2, -1/2) are applied at the flush
+  const float2 u = __fmul2_rn(pk2(vg0 ? oG.x : 0.0f, vg1 ? oG.y : 0.0f), dla);
+  const float2 tx = __fmul2_rn(u, __ffma2_rn(bc2(r0.w), dy, bc2(adx)));  // u (a dx + b dy)
+  const float2 ty = __fmul2_rn(u, __ffma2_rn(bc2(r1.x), dy, bc2(bdx)));  // u (c dy + b dx)
+  p[kMx] = tx.x + tx.y;
+  p[kMy] = ty.x + ty.y;
+  p[kMxAbs] = fabsf(tx.x) + fabsf(tx.y);
+  p[kMyAbs] = fabsf(ty.x) + fabsf(ty.y);
+  const float2 udy = __fmul2_rn(u, dy);
+  const float usum = u.x + u.y;
+  p[kCx] = usum * dx * dx;
+  p[kCy] = (udy.x + udy.y) * dx;
+  p[kCw] = fmaf(udy.x, dy.x, udy.y * dy.y);
+  const float2 og = __fmul2_rn(pk2(vg0 ? G.x : 0.0f, vg1 ? G.y : 0.0f), dla);
+  p[kOp] = og.x + og.y;
+}
+
 // splats staged per CTA: one bucket (config 3, B200: 1.17 ms; 2 buckets 1.19,
 // 4 buckets 1.24, 8 buckets 1.26)
 constexpr int kChunk = 32;
@@ -308,6 +378,7 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
           v[k] = (msk[k] >> jj) & 1u;
+          if constexpr (PX == 2) continue;  // the packed path below evaluates the pair
           dx[k] = r0.x - pfx[k];
           dy[k] = r0.y - pfy[k];
           const float power =
@@ -350,6 +421,19 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
         if (__ballot_sync(0xffffffffu, any) == 0u) continue;  // warp-uniform
       }
       float p[kSlots];
+      if constexpr (kMask && PX == 2) {
+        // the thread's two pixels share a column (dx) and sit two rows apart:
+        // their arithmetic runs as packed pairs (one f32x2 instruction per two
+        // lanes' worth of work on the issue-bound pipe)
+        float2 T2 = pk2(T[0], T[1]), ad2 = pk2(adot[0], adot[1]);
+        mask_pair_partials(p, r0, r1, r2, v[0], v[1], pfx[0], pk2(-pfy[0], -pfy[1]), T2, ad2,
+                           pk2(d0[0], d0[1]), pk2(d1[0], d1[1]), pk2(d2[0], d2[1]),
+                           pk2(-tfbg[0], -tfbg[1]));
+        T[0] = T2.x;
+        T[1] = T2.y;
+        adot[0] = ad2.x;
+        adot[1] = ad2.y;
+      } else {
 #pragma unroll
       for (int q = 0; q < kSlots; ++q) p[q] = 0.0f;
       const float c0c = r1.z, c1c = r1.w, c2c = r2.x;
@@ -378,6 +462,7 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
         p[kCy] += udx * dy[k];
         p[kCw] += u * dy[k] * dy[k];
         p[kOp] += (vg[k] ? G[k] : 0.0f) * dL_dalpha;
+      }
       }
       int slot;
       const float tot = warp_transpose_sum11(p, lane, slot);
