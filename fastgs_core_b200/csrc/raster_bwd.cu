@@ -201,6 +201,9 @@ __device__ __forceinline__ void mask_pair_partials(float (&p)[kSlots], const flo
 // 4 buckets 1.24, 8 buckets 1.26)
 constexpr int kChunk = 32;
 constexpr int kBwdPixelsPerThread = 2;
+// contribution-mask path with packed pixel pairs (config 3: 0.855 ms; four
+// pixels per thread 0.967 ms)
+constexpr int kBwdMaskPx = 2;
 
 // One CTA per group of kGroupBuckets consecutive buckets of the global bucket
 // list (kChunk splats at most), so that every CTA carries the same bounded work
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
 #pragma unroll
         for (int k = 0; k < PX; ++k) {
           v[k] = (msk[k] >> jj) & 1u;
-          if constexpr (PX == 2) continue;  // the packed path below evaluates the pair
+          if constexpr (PX % 2 == 0) continue;  // the packed path below evaluates the pairs
           dx[k] = r0.x - pfx[k];
           dy[k] = r0.y - pfy[k];
           const float power =
@@ -421,18 +424,27 @@ __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
         if (__ballot_sync(0xffffffffu, any) == 0u) continue;  // warp-uniform
       }
       float p[kSlots];
-      if constexpr (kMask && PX == 2) {
-        // the thread's two pixels share a column (dx) and sit two rows apart:
-        // their arithmetic runs as packed pairs (one f32x2 instruction per two
+      if constexpr (kMask && PX % 2 == 0) {
+        // a thread's pixels share a column (dx) and sit two rows apart: their
+        // arithmetic runs as packed pairs (one f32x2 instruction per two
         // lanes' worth of work on the issue-bound pipe)
-        float2 T2 = pk2(T[0], T[1]), ad2 = pk2(adot[0], adot[1]);
-        mask_pair_partials(p, r0, r1, r2, v[0], v[1], pfx[0], pk2(-pfy[0], -pfy[1]), T2, ad2,
-                           pk2(d0[0], d0[1]), pk2(d1[0], d1[1]), pk2(d2[0], d2[1]),
-                           pk2(-tfbg[0], -tfbg[1]));
-        T[0] = T2.x;
-        T[1] = T2.y;
-        adot[0] = ad2.x;
-        adot[1] = ad2.y;
+#pragma unroll
+        for (int k = 0; k < PX; k += 2) {
+          float2 T2 = pk2(T[k], T[k + 1]), ad2 = pk2(adot[k], adot[k + 1]);
+          float pk[kSlots];
+          mask_pair_partials(k == 0 ? p : pk, r0, r1, r2, v[k], v[k + 1], pfx[0],
+                             pk2(-pfy[k], -pfy[k + 1]), T2, ad2, pk2(d0[k], d0[k + 1]),
+                             pk2(d1[k], d1[k + 1]), pk2(d2[k], d2[k + 1]),
+                             pk2(-tfbg[k], -tfbg[k + 1]));
+          if (k > 0) {
+#pragma unroll
+            for (int q = 0; q < kSlots; ++q) p[q] += pk[q];
+          }
+          T[k] = T2.x;
+          T[k + 1] = T2.y;
+          adot[k] = ad2.x;
+          adot[k + 1] = ad2.y;
+        }
       } else {
 #pragma unroll
       for (int q = 0; q < kSlots; ++q) p[q] = 0.0f;
@@ -553,7 +565,7 @@ int fgs_rasterize_backward(const fgs_raster_params* p, const uint32_t* ranges,
   a.contrib_mask = p->contrib_mask;
   a.sparse = p->sparse_samples != 0;
   if (a.contrib_mask)
-    raster_bwd_kernel<kBwdPixelsPerThread, true><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
+    raster_bwd_kernel<kBwdMaskPx, true><<<(unsigned)groups, kTilePx / kBwdMaskPx, 0, s>>>(a);
   else
     raster_bwd_kernel<kBwdPixelsPerThread, false><<<(unsigned)groups, kTilePx / kBwdPixelsPerThread, 0, s>>>(a);
   return check_launch("rasterize_backward");
