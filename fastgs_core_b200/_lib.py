@@ -65,6 +65,8 @@ _SIGS = {
     "fgs_preprocess_backward_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 11
                                       + [_i32, _p, _p, _p]),
     "fgs_preprocess_forward_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 15),
+    "fgs_preprocess_forward_train_geometry": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 12),
+    "fgs_preprocess_colors_train": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 6),
     "fgs_preprocess_backward_adam": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 14
                                      + [_f, _f, _f, _i32, _i32, _p, _p]),
     "fgs_loss_scratch_bytes": (_sz, [_i32, _i32]),
@@ -76,6 +78,7 @@ _SIGS = {
                                           C.POINTER(_f), _f, _f, _f, _i32, _i32, _p]),
     "fgs_adam_step_peers": (C.c_int, [_i64, _i32, _i32, C.POINTER(_p), C.POINTER(_p), _p, _p, _i32,
                                       C.POINTER(_i64), C.POINTER(_f), _f, _f, _f, _i32, _i32, _p]),
+    "fgs_set_exchange_grid": (C.c_int, [_i32]),
     "fgs_metric_map": (C.c_int, [_i64, _p, _p, _f, _p, _p, _p, _p]),
     "fgs_score_accumulate": (C.c_int, [_i64, _p, _p, _i64, _p, _p, _p]),
     "fgs_score_finalize": (C.c_int, [_i64, _p, _p, _i32, _p, _p, _p, _p]),

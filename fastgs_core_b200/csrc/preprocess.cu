@@ -66,6 +66,7 @@ struct PreArgs {
   uint32_t* tiles;
   uint8_t* clamped;
   float* vs_out;
+  int skip_color;  // geometry only: rgb and clamped are neither computed nor written
 };
 
 // Stage `count` floats starting at g (16-byte aligned chunk boundaries are
@@ -143,13 +144,14 @@ __device__ __forceinline__ v3 sh_color(int deg, v3 dir_unnorm, const float* dcp,
 }
 
 template <bool kRaw>
+// eight resident CTAs per SM (config 3: 0.101 ms; four: 0.112 ms)
 __global__ void __launch_bounds__(kPreThreads, 8) preprocess_fwd_kernel(PreArgs a) {
   extern __shared__ float s_sh[];
   const fgs_preprocess_params& p = a.p;
   const int base = blockIdx.x * kPreThreads;
   const int i = base + threadIdx.x;
   const int S3 = p.max_sh_coeffs * 3;
-  const bool use_sh = !p.use_colors_precomp && p.degree > 0 && p.max_sh_coeffs > 0;
+  const bool use_sh = !a.skip_color && !p.use_colors_precomp && p.degree > 0 && p.max_sh_coeffs > 0;
   if (use_sh) {
     const int cnt = min(kPreThreads, p.n - base);
     stage_floats(s_sh, a.sh + (int64_t)base * S3, (int64_t)cnt * S3);
@@ -232,7 +234,8 @@ __global__ void __launch_bounds__(kPreThreads, 8) preprocess_fwd_kernel(PreArgs 
       const float img_y = ((pp_y + 1.0f) * (float)p.image_height - 1.0f) * 0.5f;
       const uint32_t tc = tile_walk(img_x, img_y, co, a.gx, a.gy, p.mult, [](int) {});
       if (tc != 0u) {
-        if (p.use_colors_precomp) {
+        if (a.skip_color) {
+        } else if (p.use_colors_precomp) {
 #pragma unroll
           for (int c = 0; c < 3; ++c) rgb_out[c] = a.colors_precomp[3 * (int64_t)i + c];
         } else {
@@ -258,15 +261,55 @@ __global__ void __launch_bounds__(kPreThreads, 8) preprocess_fwd_kernel(PreArgs 
   a.depths[i] = depth_out;
   reinterpret_cast<float4*>(a.conic)[i] = conic_out;
   reinterpret_cast<float4*>(a.vs_out)[i] = vs_o;
+  if (!a.skip_color) {
 #pragma unroll
-  for (int c = 0; c < 3; ++c) {
-    a.rgb[3 * (int64_t)i + c] = rgb_out[c];
-    a.clamped[3 * (int64_t)i + c] = cl[c];
+    for (int c = 0; c < 3; ++c) {
+      a.rgb[3 * (int64_t)i + c] = rgb_out[c];
+      a.clamped[3 * (int64_t)i + c] = cl[c];
+    }
   }
   float2* cv = reinterpret_cast<float2*>(a.cov3d + 6 * (int64_t)i);
   cv[0] = make_float2(c3[0], c3[1]);
   cv[1] = make_float2(c3[2], c3[3]);
   cv[2] = make_float2(c3[4], c3[5]);
+}
+
+// Colour step of the training preprocess on its own: the SH colour (degree
+// `degree`, 15 rest coefficients per Gaussian staged through shared memory)
+// of every Gaussian that touches a tile, zeros and no clamp flags elsewhere;
+// the same operations as preprocess_fwd_kernel<true>, so the same bits.
+__global__ void __launch_bounds__(kPreThreads) color_train_kernel(int64_t n, int degree,
+                                                                 const float* __restrict__ raw,
+                                                                 const float* __restrict__ cam_pos,
+                                                                 const uint32_t* __restrict__ tiles,
+                                                                 float* __restrict__ rgb,
+                                                                 uint8_t* __restrict__ clamped) {
+  extern __shared__ float s_sh[];
+  constexpr int S3 = 45;
+  const int64_t base = (int64_t)blockIdx.x * kPreThreads;
+  const int64_t i = base + threadIdx.x;
+  const bool use_sh = degree > 0;
+  if (use_sh) {
+    const int cnt = (int)min((int64_t)kPreThreads, n - base);
+    stage_floats(s_sh, raw + 6 * n + base * S3, (int64_t)cnt * S3);
+    __syncthreads();
+  }
+  if (i >= n) return;
+  float o[3] = {0.f, 0.f, 0.f};
+  uint8_t cl[3] = {0, 0, 0};
+  if (tiles[i] != 0u) {
+    const v3 d = V3(raw[3 * i] - cam_pos[0], raw[3 * i + 1] - cam_pos[1], raw[3 * i + 2] - cam_pos[2]);
+    const float* shp = use_sh ? (s_sh + threadIdx.x * S3) : nullptr;
+    const v3 col = sh_color(use_sh ? degree : 0, d, raw + 3 * n + 3 * i, shp, cl);
+    o[0] = col.x;
+    o[1] = col.y;
+    o[2] = col.z;
+  }
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    rgb[3 * i + c] = o[c];
+    clamped[3 * i + c] = cl[c];
+  }
 }
 
 // ------------------------------------------------------------ prefix sum
@@ -937,21 +980,22 @@ int fgs_preprocess_forward(const fgs_preprocess_params* p, const float* means3d,
   return check_launch("preprocess_forward");
 }
 
-int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const float* params,
-                                 const float* viewmatrix, const float* projmatrix,
-                                 const float* cam_pos, const float* viewspace_in, int32_t* radii,
-                                 float* xys, float* depths, float* cov3d, float* rgb,
-                                 float* conic_opacity, uint32_t* tiles_touched, uint8_t* clamped,
-                                 float* viewspace_out, void* stream) {
+static int launch_forward_train(const fgs_preprocess_params* p, const float* params,
+                                const float* viewmatrix, const float* projmatrix,
+                                const float* cam_pos, const float* viewspace_in, int32_t* radii,
+                                float* xys, float* depths, float* cov3d, float* rgb,
+                                float* conic_opacity, uint32_t* tiles_touched, uint8_t* clamped,
+                                float* viewspace_out, bool color, void* stream) {
   int st = validate_pre(p);
   if (st) return st;
   if (p->n == 0) return FGS_OK;
   FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
                 "training mode needs the scales+quats and dc+sh paths");
   FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
-  FGS_CHECK_ARG(params && viewmatrix && projmatrix && cam_pos && viewspace_in, "missing input pointer");
-  FGS_CHECK_ARG(radii && xys && depths && cov3d && rgb && conic_opacity && tiles_touched &&
-                    clamped && viewspace_out,
+  FGS_CHECK_ARG(params && viewmatrix && projmatrix && viewspace_in && (cam_pos || !color),
+                "missing input pointer");
+  FGS_CHECK_ARG(radii && xys && depths && cov3d && conic_opacity && tiles_touched &&
+                    viewspace_out && ((rgb && clamped) || !color),
                 "missing output pointer");
   FGS_CHECK_ARG(FGS_ALIGNED(xys, 8) && FGS_ALIGNED(cov3d, 8) && FGS_ALIGNED(conic_opacity, 16) &&
                     FGS_ALIGNED(viewspace_out, 16),
@@ -969,13 +1013,57 @@ int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const float* pa
   a.viewmatrix = viewmatrix; a.projmatrix = projmatrix; a.cam_pos = cam_pos; a.vs_in = viewspace_in;
   a.radii = radii; a.xys = xys; a.depths = depths; a.cov3d = cov3d; a.rgb = rgb;
   a.conic = conic_opacity; a.tiles = tiles_touched; a.clamped = clamped; a.vs_out = viewspace_out;
-  const bool use_sh = p->degree > 0;
+  a.skip_color = color ? 0 : 1;
+  const bool use_sh = color && p->degree > 0;
   const size_t smem = use_sh ? (size_t)kPreThreads * p->max_sh_coeffs * 3 * sizeof(float) : 0;
   static unsigned long long attr_done = 0;
   if (smem > 48 * 1024) smem_attr_once(preprocess_fwd_kernel<true>, (int)smem, &attr_done);
   const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
   preprocess_fwd_kernel<true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
-  return check_launch("preprocess_forward_train");
+  return check_launch(color ? "preprocess_forward_train" : "preprocess_forward_train_geometry");
+}
+
+int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const float* params,
+                                 const float* viewmatrix, const float* projmatrix,
+                                 const float* cam_pos, const float* viewspace_in, int32_t* radii,
+                                 float* xys, float* depths, float* cov3d, float* rgb,
+                                 float* conic_opacity, uint32_t* tiles_touched, uint8_t* clamped,
+                                 float* viewspace_out, void* stream) {
+  return launch_forward_train(p, params, viewmatrix, projmatrix, cam_pos, viewspace_in, radii, xys,
+                              depths, cov3d, rgb, conic_opacity, tiles_touched, clamped,
+                              viewspace_out, true, stream);
+}
+
+int fgs_preprocess_forward_train_geometry(const fgs_preprocess_params* p, const float* params,
+                                          const float* viewmatrix, const float* projmatrix,
+                                          const float* viewspace_in, int32_t* radii, float* xys,
+                                          float* depths, float* cov3d, float* conic_opacity,
+                                          uint32_t* tiles_touched, float* viewspace_out,
+                                          void* stream) {
+  return launch_forward_train(p, params, viewmatrix, projmatrix, nullptr, viewspace_in, radii, xys,
+                              depths, cov3d, nullptr, conic_opacity, tiles_touched, nullptr,
+                              viewspace_out, false, stream);
+}
+
+int fgs_preprocess_colors_train(const fgs_preprocess_params* p, const float* params,
+                                const float* cam_pos, const uint32_t* tiles_touched, float* rgb,
+                                uint8_t* clamped, void* stream) {
+  int st = validate_pre(p);
+  if (st) return st;
+  if (p->n == 0) return FGS_OK;
+  FGS_CHECK_ARG(!p->use_colors_precomp && p->max_sh_coeffs == 15,
+                "training mode stores dc + 15 SH rest coefficients");
+  FGS_CHECK_ARG(p->degree >= 0 && p->degree <= 3, "degree must be in [0, 3]");
+  FGS_CHECK_ARG(params && cam_pos && tiles_touched && rgb && clamped, "missing pointer");
+  const size_t smem = p->degree > 0 ? (size_t)kPreThreads * 45 * sizeof(float) : 0;
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(color_train_kernel, (int)smem, &attr_done);
+  const int64_t n = p->n;
+  const unsigned blocks = (unsigned)((n + kPreThreads - 1) / kPreThreads);
+  color_train_kernel<<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(n, p->degree, params,
+                                                                         cam_pos, tiles_touched,
+                                                                         rgb, clamped);
+  return check_launch("preprocess_colors_train");
 }
 
 size_t fgs_scan_scratch_bytes(int64_t n) {

@@ -629,6 +629,8 @@ __global__ void init_pair_kernel(unsigned int* p, unsigned int a, unsigned int b
   p[1] = b;
 }
 
+// grid budget of the exchange kernels (resident CTAs per SM; 0: their defaults)
+static int g_exchange_bps = 0;
 static bool g_win_ready[64] = {false};  // per device: c_win lives in each device's constant bank
 static int ensure_window() {
   int dev = 0;
@@ -747,6 +749,12 @@ int fgs_adam_step(int64_t total, float* params, const float* grads, float* exp_a
   return check_launch("adam_step");
 }
 
+int fgs_set_exchange_grid(int32_t blocks_per_sm) {
+  FGS_CHECK_ARG(blocks_per_sm >= 0 && blocks_per_sm <= 8, "blocks_per_sm must be in [0, 8]");
+  g_exchange_bps = blocks_per_sm;
+  return FGS_OK;
+}
+
 int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, float* const* params_ranks,
                         const float* const* grads_ranks, float* exp_avg, float* exp_avg_sq,
                         int32_t num_groups, const int64_t* group_end, const float* group_lr,
@@ -787,7 +795,8 @@ int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, float* const
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t n4 = shard / 4;
   const int64_t want = (n4 + 255) / 256;
-  const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  const int64_t cap = (int64_t)sms * (g_exchange_bps > 0 ? g_exchange_bps : 8);
+  const int blocks = (int)(want < cap ? want : cap);
   adam_peers_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(n4, world, rank, pp, exp_avg,
                                                               exp_avg_sq, g, beta1, beta2, eps,
                                                               bc1, bc2);
@@ -825,7 +834,8 @@ int fgs_adam_step_multicast(int64_t shard, const float* params_local, float* par
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t n4 = shard / 4;
   const int64_t want = (n4 + 255) / 256;
-  const int blocks = (int)(want < (int64_t)sms * 4 ? want : (int64_t)sms * 4);
+  const int64_t cap = (int64_t)sms * (g_exchange_bps > 0 ? g_exchange_bps : 4);
+  const int blocks = (int)(want < cap ? want : cap);
   adam_nvls_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
       n4, params_local, params_mc, grads_mc, exp_avg, exp_avg_sq, g, beta1, beta2, eps, bc1, bc2);
   return check_launch("adam_step_multicast");

@@ -94,6 +94,7 @@ def _apply_rows(tr, param_index: np.ndarray, moment_index: np.ndarray, keep_stat
 def prune_points(tr, prune_mask: np.ndarray, score: np.ndarray | None = None):
     """prune_points (scripts/train_scanner_fastgs.py:510-537). Returns the
     pruned score array (or None)."""
+    tr.settle()
     prune_mask = np.asarray(prune_mask, bool)
     if prune_mask.size == 0 or not np.any(prune_mask):
         return score
@@ -116,6 +117,7 @@ def _append_copies(tr, sources: np.ndarray, score):
 
 def densify_and_clone(tr, metric_mask, clone_filter, score=None):
     """densify_and_clone_fastgs (:540-566)."""
+    tr.settle()
     selected = np.asarray(metric_mask, bool) & np.asarray(clone_filter, bool)
     if not np.any(selected):
         return 0, score
@@ -125,6 +127,7 @@ def densify_and_clone(tr, metric_mask, clone_filter, score=None):
 
 def densify_and_split(tr, metric_mask, split_filter, rng, split_factor: int, score=None):
     """densify_and_split_fastgs (:569-618)."""
+    tr.settle()
     selected = np.asarray(metric_mask, bool) & np.asarray(split_filter, bool)
     if selected.size < tr.n:
         selected = np.concatenate([selected, np.zeros(tr.n - selected.size, bool)])
@@ -152,6 +155,7 @@ def cap_opacity_logits(tr, opacity_cap: float):
     """cap_opacity_logits (:621-638): logit(min(opacity, cap)); the opacity
     moments restart at zero (with sharded moments: this rank's part of the
     opacity segment)."""
+    tr.settle()
     sharded = tr.world > 1
     check(lib().fgs_opacity_cap(tr.n, float(opacity_cap), _p(tr.params_pad),
                                 None if sharded else _p(tr.exp_avg),
@@ -166,6 +170,7 @@ def cap_opacity_logits(tr, opacity_cap: float):
 
 def reset_opacity_logits(tr, reset_value: float):
     """reset_opacity_logits (:640-658): the same operation as the cap."""
+    tr.settle()
     cap_opacity_logits(tr, reset_value)
 
 
@@ -182,6 +187,7 @@ def densify_and_prune_fastgs(tr, args: DensifyArgs, scene_extent: float, importa
     every rank's views (tr.global_stats(); the trainer's own with one rank).
     With several ranks every rank calls it with the same scores and an
     equally seeded generator, so all make the same choices."""
+    tr.settle()
     imp = torch.as_tensor(np.asarray(importance_score, np.float32), device=tr.dev)
     gstats = tr.global_stats() if tr.world > 1 else tr.stats
     mk = _masks(tr, "fgs_densify_masks", _p(tr.params_pad), _p(gstats), _p(imp),
@@ -238,6 +244,7 @@ def compute_gaussian_scores_fastgs(tr, cams, targets, camera_indices, loss_thres
     densify, pruning = min-max normalised sum of photometric loss x counts).
     targets[i] is the [3, H*W] float32 device target of cams[i]. Returns
     (importance or None, pruning) as numpy arrays."""
+    tr.settle()
     L = lib()
     n, dev = tr.n, tr.dev
     st = torch.cuda.current_stream(dev).cuda_stream
@@ -278,6 +285,7 @@ def compute_gaussian_scores_fastgs(tr, cams, targets, camera_indices, loss_thres
 def final_prune_fastgs(tr, min_opacity: float, pruning_score, score_thresh: float,
                        min_gaussians: int) -> dict:
     """final_prune_fastgs (:748-795)."""
+    tr.settle()
     n = tr.n
     logits = tr.params[51 * n:52 * n].cpu().numpy()
     opacities = (1.0 / (1.0 + np.exp(-logits))).astype(np.float32)

@@ -233,6 +233,19 @@ class Trainer:
         ends = np.clip(np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n - self._lo, 0,
                        self._hi - self._lo)
         self._group_end = (C.c_int64 * 6)(*ends.tolist())
+        # With several ranks and a symmetric-memory exchange, the SH rest
+        # coefficients (45 of the 59 floats) are exchanged after the rest of
+        # the buffer, while the next render's geometry and binning run on a
+        # second stream; that render's colour step waits for them. Everything
+        # a caller queues on its own stream after step() sees the whole update.
+        self.overlap = (self._symm is not None
+                        and os.environ.get("FGS_OVERLAP_EXCHANGE", "1") != "0")
+        self._geo_stream = torch.cuda.Stream(device=d, priority=-1) if self.overlap else None
+        self.rest_blocks_per_sm = int(os.environ.get("FGS_REST_BLOCKS_PER_SM", "2"))
+        self._e_front = torch.cuda.Event()  # every rank's non-SH parameters landed
+        self._front_pending = False
+        self._geo_done = torch.cuda.Event()
+        self._set_pieces()
         # instrumentation: CUDA events around chosen launches (same stream),
         # and a count of this library's kernel launches
         self.record = set()
@@ -265,6 +278,7 @@ class Trainer:
     def full_moments(self) -> tuple[torch.Tensor, torch.Tensor]:
         """Adam moments of every flat element (59 n floats each): this rank's
         shards, all-gathered when the moments are sharded over ranks."""
+        self.settle()
         total = FLOATS_PER_GAUSSIAN * self.n
         if self.world == 1:
             return self.exp_avg[:total], self.exp_avg_sq[:total]
@@ -287,6 +301,7 @@ class Trainer:
         moments (the decisions are made on global statistics with one
         generator): each keeps its shard of the moments, and the symmetric
         parameter and gradient buffers are allocated and registered anew."""
+        self.settle()
         d = self.dev
         total = FLOATS_PER_GAUSSIAN * n_new
         self.n = n_new
@@ -300,6 +315,7 @@ class Trainer:
         if self._symm is not None:
             self.params_pad, self.grads_pad, self._hp, self._hg = self._symm
         else:
+            self.overlap = False
             self.params_pad = torch.empty(padded, device=d)
             self.grads_pad = torch.empty(padded, device=d)
         self.params_pad.zero_()
@@ -320,13 +336,55 @@ class Trainer:
         ends = np.clip(np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n_new - self._lo, 0,
                        self._hi - self._lo)
         self._group_end = (C.c_int64 * 6)(*ends.tolist())
+        self._set_pieces()
         self._vs_zeroed = False
 
     # kernels each C entry point launches (memsets are not kernels)
-    _KERNELS = {"preprocess": 1, "depth_order": 8, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
+    _KERNELS = {"colors": 1, "preprocess": 1, "depth_order": 8, "scan": 3, "duplicate": 1, "tile_prep": 2, "tile_order": 1, "rasterize_forward": 1,
                 "loss": 2, "rasterize_backward": 1, "preprocess_backward_train": 1,
                 "preprocess_backward_adam": 1, "activate": 1,
                 "adam": 1}
+
+    def settle(self) -> None:
+        """Close the overlap window of the last step: the next render then
+        starts after everything queued on the caller's stream (densification,
+        opacity resets, checkpoint loads), not only after the exchange's
+        non-SH part."""
+        self._front_pending = False
+
+    def _set_pieces(self) -> None:
+        """Split this rank's shard [0, per) into the part before the SH rest
+        segment, the SH rest segment [6n, 51n) (rounded inwards to 16-byte
+        boundaries) and the part after it, each with its own group table."""
+        n, lo, per = self.n, self._lo, self._per
+        rs = min(max(-(-6 * n // 4) * 4 - lo, 0), per)
+        re = max(min(max((51 * n // 4) * 4 - lo, 0), per), rs)
+        shard_ends = np.clip(np.array([3, 6, 51, 52, 55, 59], dtype=np.int64) * n - lo, 0,
+                             self._hi - lo)
+        self._pieces = []
+        for off, ln in ((0, rs), (rs, re - rs), (re, per - re)):
+            ends = np.clip(shard_ends - off, 0, ln)
+            self._pieces.append((off, ln, (C.c_int64 * 6)(*ends.tolist())))
+
+    def _exchange(self, off, length, group_end, lrs, b1, b2):
+        """Fused exchange + Adam of shard elements [off, off + length)."""
+        if length <= 0:
+            return
+        o4 = (self._lo + off) * 4
+        if self.comm == "multicast":
+            self._call("adam", lib().fgs_adam_step_multicast, length,
+                       _p(self.params_pad[self._lo + off:]),
+                       C.c_void_p(self._hp.multicast_ptr + o4),
+                       C.c_void_p(self._hg.multicast_ptr + o4), _p(self.exp_avg[off:]),
+                       _p(self.exp_avg_sq[off:]), 6, group_end, lrs, b1, b2, self.eps,
+                       self.step_count, int(self.bias_correction), self._stream())
+        else:
+            world = self.world
+            pp = (C.c_void_p * world)(*[self._hp.buffer_ptrs[r] + o4 for r in range(world)])
+            gp = (C.c_void_p * world)(*[self._hg.buffer_ptrs[r] + o4 for r in range(world)])
+            self._call("adam", lib().fgs_adam_step_peers, length, world, self.rank, pp, gp,
+                       _p(self.exp_avg[off:]), _p(self.exp_avg_sq[off:]), 6, group_end, lrs, b1,
+                       b2, self.eps, self.step_count, int(self.bias_correction), self._stream())
 
     def _call(self, name, fn, *args):
         ev = None
@@ -397,7 +455,18 @@ class Trainer:
         P = W * H
         gx, gy = tile_grid(W, H)
         T = gx * gy
-        st = self._stream()
+        main = torch.cuda.current_stream(d)
+        # geometry and binning on the second stream while the previous step's
+        # SH exchange finishes on this one (multi-rank overlap); else here
+        split = self.overlap
+        geo = main
+        if split and self._front_pending:
+            geo = self._geo_stream
+            geo.wait_event(self._e_front)
+            self._front_pending = False
+        st = C.c_void_p(geo.cuda_stream)
+        gctx = torch.cuda.stream(geo)
+        gctx.__enter__()
         # camera upload on the side stream into one of two device slots: the
         # slot's previous user (two views back) and the pinned staging's last
         # copy are complete, because the host has since waited on a later
@@ -408,7 +477,7 @@ class Trainer:
         hc[0:16] = cam.viewmatrix.reshape(-1)
         hc[16:32] = cam.projmatrix.reshape(-1)
         hc[32:35] = cam.campos.reshape(-1)
-        cur = torch.cuda.current_stream(d)
+        cur = geo
         with torch.cuda.stream(self._k_stream):
             cm.copy_(self._cam_host, non_blocking=True)
             self._cam_ready.record(self._k_stream)
@@ -431,9 +500,14 @@ class Trainer:
         clamped = ws.get("clamped", 3 * n, torch.uint8)
         vs_out = ws.get("vs_out", 4 * n, torch.float32)
         # activations (sigmoid, exp, normalise) are applied inside the kernels
-        self._call("preprocess", L.fgs_preprocess_forward_train, C.byref(prm), _p(self.params), _p(vm),
-                   _p(pm), _p(cp), _p(vs_in), _p(radii), _p(xys), _p(depths), _p(cov3d), _p(rgb),
-                   _p(conic), _p(tiles), _p(clamped), _p(vs_out), st)
+        if split:
+            self._call("preprocess", L.fgs_preprocess_forward_train_geometry, C.byref(prm),
+                       _p(self.params), _p(vm), _p(pm), _p(vs_in), _p(radii), _p(xys), _p(depths),
+                       _p(cov3d), _p(conic), _p(tiles), _p(vs_out), st)
+        else:
+            self._call("preprocess", L.fgs_preprocess_forward_train, C.byref(prm), _p(self.params),
+                       _p(vm), _p(pm), _p(cp), _p(vs_in), _p(radii), _p(xys), _p(depths),
+                       _p(cov3d), _p(rgb), _p(conic), _p(tiles), _p(clamped), _p(vs_out), st)
         cap = self._key_cap
         kb = sort_key_bits(T)
         # depth-first binning: order the Gaussians by depth, emit keys in that
@@ -503,6 +577,16 @@ class Trainer:
             self._call("sort", L.fgs_sort_pairs_bits, K, sort_lo, kb, *kp, sws_n, st)
             slot[1:2].copy_(kbufs[4][:4].view(torch.int32), non_blocking=True)
         self._flag_views.append(self._views - 1)
+        gctx.__exit__(None, None, None)
+        if geo is not main:
+            self._geo_done.record(geo)
+            main.wait_event(self._geo_done)
+        cur, st = main, C.c_void_p(main.cuda_stream)
+        if split:
+            # colours from the SH coefficients, which the previous step's
+            # exchange has finished writing on this stream
+            self._call("colors", L.fgs_preprocess_colors_train, C.byref(prm), _p(self.params),
+                       _p(cp), _p(tiles), _p(rgb), _p(clamped), st)
         if target is not None:
             # the raster-gradient accumulators are zeroed on the side stream
             # while this stream sorts and renders (every earlier use of them
@@ -622,6 +706,7 @@ class Trainer:
         rank adopts the parameters and its shard of the moments; the
         statistics go to rank 0 (the others start at zero, so their sum and
         maximum over ranks are the saved ones)."""
+        self.settle()
         d = self.dev
         n = int(state["n"])
         total = FLOATS_PER_GAUSSIAN * n
@@ -653,6 +738,7 @@ class Trainer:
         """Activated copies of the parameters (self.opacities, self.scales,
         self.quats) for callers that want them; the step's own kernels apply
         the activations to the raw parameters themselves."""
+        self.settle()
         self._call("activate", lib().fgs_activate_params, self.n, _p(self.params), _p(self.opacities),
                    _p(self.scales), _p(self.quats), self._stream())
 
@@ -694,20 +780,24 @@ class Trainer:
             # gradient writes against peers still reading these)
             ev = self._begin("exchange")
             self._hp.barrier(channel=0)
-            off = lo * 4
-            if self.comm == "multicast":
-                self._call("adam", lib().fgs_adam_step_multicast, self._per, _p(self.params_pad[lo:]),
-                           C.c_void_p(self._hp.multicast_ptr + off),
-                           C.c_void_p(self._hg.multicast_ptr + off), _p(self.exp_avg),
-                           _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2, self.eps,
-                           self.step_count, int(self.bias_correction), self._stream())
+            if self.overlap:
+                # the non-SH parts first; the next render's geometry starts
+                # once every rank has them, while the SH rest part moves
+                front, rest, back = self._pieces
+                self._exchange(front[0], front[1], front[2], lrs, b1, b2)
+                self._exchange(back[0], back[1], back[2], lrs, b1, b2)
+                self._hp.barrier(channel=1)
+                self._e_front.record(torch.cuda.current_stream(self.dev))
+                self._front_pending = True
+                # a small grid, so that the next render's geometry kernels
+                # find free SMs while this one strides over the SH shard
+                check(lib().fgs_set_exchange_grid(self.rest_blocks_per_sm), "set_exchange_grid")
+                self._exchange(rest[0], rest[1], rest[2], lrs, b1, b2)
+                check(lib().fgs_set_exchange_grid(0), "set_exchange_grid")
+                self._hp.barrier(channel=2)
             else:
-                pp = (C.c_void_p * world)(*[self._hp.buffer_ptrs[r] + off for r in range(world)])
-                gp = (C.c_void_p * world)(*[self._hg.buffer_ptrs[r] + off for r in range(world)])
-                self._call("adam", lib().fgs_adam_step_peers, self._per, world, rank, pp, gp,
-                           _p(self.exp_avg), _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2,
-                           self.eps, self.step_count, int(self.bias_correction), self._stream())
-            self._hp.barrier(channel=1)
+                self._exchange(0, self._per, self._group_end, lrs, b1, b2)
+                self._hp.barrier(channel=1)
             self._end("exchange", ev)
             return len(mine)
         if world > 1:

@@ -376,6 +376,26 @@ FGS_API int fgs_preprocess_forward_train(const fgs_preprocess_params* p, const f
                                          int32_t* radii, float* xys, float* depths, float* cov3d,
                                          float* rgb, float* conic_opacity, uint32_t* tiles_touched,
                                          uint8_t* clamped, float* viewspace_out, void* stream);
+/* The training preprocess forward in two launches, for a caller that wants
+ * the colour step later than the geometry (no counterpart in the reference,
+ * which evaluates colours inside its one preprocess kernel,
+ * fastgs_core/metal/fastgs_preprocess.metal:117-169, 469):
+ * fgs_preprocess_forward_train_geometry writes every output of
+ * fgs_preprocess_forward_train except rgb and clamped, and reads no SH;
+ * fgs_preprocess_colors_train then writes rgb and clamped from `params` and
+ * the same tiles_touched, bit for bit as the one-launch call would. The
+ * data-parallel trainer uses the split to exchange the SH coefficients of the
+ * previous step while the geometry and the binning of this step run. */
+FGS_API int fgs_preprocess_forward_train_geometry(const fgs_preprocess_params* p,
+                                                  const float* params, const float* viewmatrix,
+                                                  const float* projmatrix,
+                                                  const float* viewspace_in, int32_t* radii,
+                                                  float* xys, float* depths, float* cov3d,
+                                                  float* conic_opacity, uint32_t* tiles_touched,
+                                                  float* viewspace_out, void* stream);
+FGS_API int fgs_preprocess_colors_train(const fgs_preprocess_params* p, const float* params,
+                                        const float* cam_pos, const uint32_t* tiles_touched,
+                                        float* rgb, uint8_t* clamped, void* stream);
 FGS_API int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* params,
                                           const float* viewmatrix, const float* projmatrix,
                                           const float* cam_pos, const float* cov3d_fwd,
@@ -454,6 +474,15 @@ FGS_API int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, floa
                                 int32_t num_groups, const int64_t* group_end,
                                 const float* group_lr, float beta1, float beta2, float eps,
                                 int32_t step, int32_t bias_correction, void* stream);
+
+/* Grid budget of fgs_adam_step_multicast and fgs_adam_step_peers for the
+ * launches that follow in this process: at most blocks_per_sm CTAs of 256
+ * threads per SM (0 restores their defaults of 4 and 8). Both kernels stride
+ * over their shard, so a small budget leaves SMs to kernels running on other
+ * streams at the same time, at some cost in the exchange's own speed. Not
+ * synchronised between host threads (new here; no counterpart in the
+ * reference). */
+FGS_API int fgs_set_exchange_grid(int32_t blocks_per_sm);
 
 /* FastGS multi-view score pass (scripts/train_scanner_fastgs.py:262-340):
  * fgs_metric_map: per-pixel mean |pred - target| over channels, min-max

@@ -356,3 +356,54 @@ def test_driver_mse_warmup(cuda_dev):
         want = (d * d).mean() if tr.loss_mode == "mse" else d.abs().mean()
         assert abs(lo[0].item() - want.item()) < 1e-4
     assert modes == ["mse", "mse", "l1_dssim", "l1_dssim"]
+
+
+@pytest.mark.parametrize("degree", [0, 1, 3])
+def test_split_preprocess_matches_fused(degree, cuda_dev):
+    """fgs_preprocess_forward_train_geometry + fgs_preprocess_colors_train (the
+    split the data-parallel trainer uses to overlap the SH exchange) give the
+    outputs of the one-launch fgs_preprocess_forward_train bit for bit."""
+    import ctypes as C
+
+    scene, cam = S.small_scene(41, 3001, 3, 96, 64)
+    tr = Trainer(scene, cuda_dev)
+    L = _lib.lib()
+    n = scene.n
+    prm = _lib.PreprocessParams(n, degree, 15, 1.0, 1.0, float(cam.tan_fovx), float(cam.tan_fovy),
+                                cam.width, cam.height, 0, 0)
+    f = lambda: torch.from_numpy(np.concatenate([cam.viewmatrix.reshape(-1), cam.projmatrix.reshape(-1),
+                                                 cam.campos.reshape(-1)]).astype(np.float32)).to(cuda_dev)
+    cm = f()
+    vm, pm, cp = cm[0:16], cm[16:32], cm[32:35]
+    vs_in = torch.zeros(4 * n, device=cuda_dev)
+
+    def outs():
+        return dict(radii=torch.full((n,), -7, dtype=torch.int32, device=cuda_dev),
+                    xys=torch.full((2 * n,), 7.0, device=cuda_dev),
+                    depths=torch.full((n,), 7.0, device=cuda_dev),
+                    cov3d=torch.full((6 * n,), 7.0, device=cuda_dev),
+                    rgb=torch.full((3 * n,), 7.0, device=cuda_dev),
+                    conic=torch.full((4 * n,), 7.0, device=cuda_dev),
+                    tiles=torch.full((n,), 7, dtype=torch.uint32, device=cuda_dev),
+                    clamped=torch.full((3 * n,), 7, dtype=torch.uint8, device=cuda_dev),
+                    vs=torch.full((4 * n,), 7.0, device=cuda_dev))
+
+    a, b = outs(), outs()
+    s = _stream()
+    assert L.fgs_preprocess_forward_train(C.byref(prm), _p(tr.params), _p(vm), _p(pm), _p(cp), _p(vs_in),
+                                          _p(a["radii"]), _p(a["xys"]), _p(a["depths"]), _p(a["cov3d"]),
+                                          _p(a["rgb"]), _p(a["conic"]), _p(a["tiles"]), _p(a["clamped"]),
+                                          _p(a["vs"]), s) == 0
+    assert L.fgs_preprocess_forward_train_geometry(C.byref(prm), _p(tr.params), _p(vm), _p(pm), _p(vs_in),
+                                                   _p(b["radii"]), _p(b["xys"]), _p(b["depths"]),
+                                                   _p(b["cov3d"]), _p(b["conic"]), _p(b["tiles"]),
+                                                   _p(b["vs"]), s) == 0
+    # geometry alone leaves the colour outputs untouched
+    assert torch.all(b["rgb"] == 7.0) and torch.all(b["clamped"] == 7)
+    assert L.fgs_preprocess_colors_train(C.byref(prm), _p(tr.params), _p(cp), _p(b["tiles"]),
+                                         _p(b["rgb"]), _p(b["clamped"]), s) == 0
+    torch.cuda.synchronize()
+    assert (a["tiles"].view(torch.int32) != 0).sum().item() > 100
+    for k in a:
+        assert torch.equal(a[k].view(torch.uint8) if a[k].dtype != torch.uint8 else a[k],
+                           b[k].view(torch.uint8) if b[k].dtype != torch.uint8 else b[k]), k
