@@ -238,10 +238,13 @@ class Trainer:
         # the buffer, while the next render's geometry and binning run on a
         # second stream; that render's colour step waits for them. Everything
         # a caller queues on its own stream after step() sees the whole update.
+        # Off by default: at two B200s the geometry kernels slowed by as much
+        # as the exchange hid (config 3, views/s: 708.9 without; 644.0 /
+        # 700.3 / 709.6 with 1 / 2 / 4 exchange CTAs per SM).
         self.overlap = (self._symm is not None
-                        and os.environ.get("FGS_OVERLAP_EXCHANGE", "1") != "0")
+                        and os.environ.get("FGS_OVERLAP_EXCHANGE", "0") == "1")
         self._geo_stream = torch.cuda.Stream(device=d, priority=-1) if self.overlap else None
-        self.rest_blocks_per_sm = int(os.environ.get("FGS_REST_BLOCKS_PER_SM", "2"))
+        self.rest_blocks_per_sm = int(os.environ.get("FGS_REST_BLOCKS_PER_SM", "4"))
         self._e_front = torch.cuda.Event()  # every rank's non-SH parameters landed
         self._front_pending = False
         self._geo_done = torch.cuda.Event()

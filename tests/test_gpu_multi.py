@@ -11,7 +11,8 @@ that renders both views itself:
 * densification in the middle of a run: steps, densify_and_prune_fastgs on
   the all-reduced statistics with the same scores and generator on every
   rank, then more steps on the new set of Gaussians; the replicas stay
-  identical and follow the single process.
+  identical and follow the single process. Also with the SH part of the
+  exchange overlapped with the next render's geometry (FGS_OVERLAP_EXCHANGE).
 """
 import datetime
 import os
@@ -87,6 +88,9 @@ def _worker(rank, port, comm, mode, eps, q):
     from fastgs_core_b200.train import Trainer
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_DEBUG="WARN")
+    # "<comm>+overlap": the SH exchange overlapped with the next render's geometry
+    comm, _, ov = comm.partition("+")
+    os.environ["FGS_OVERLAP_EXCHANGE"] = "1" if ov == "overlap" else "0"
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
@@ -170,14 +174,14 @@ def test_two_rank_step_matches_single_process(comm):
     assert big.float().mean() > 0.3
 
 
-@pytest.mark.parametrize("comm", ["multicast", "p2p", "nccl"])
+@pytest.mark.parametrize("comm", ["multicast", "p2p", "nccl", "multicast+overlap", "p2p+overlap"])
 def test_two_rank_densify_matches_single_process(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     # eps = 1: Adam's update is linear in the gradient, so the two runs' float
     # noise does not grow into different sign decisions over the steps
     res = _spawn(comm, "densify", 1.0)
-    if comm != "nccl" and res[0][1] != comm:
+    if comm != "nccl" and res[0][1] != comm.partition("+")[0]:
         pytest.skip("symmetric memory (NVLink multicast / peer mappings) unavailable on this box")
     _, want_res, (_, n, want_p, want_m, want_v, want_s) = _single("densify", 1.0)
     assert want_res["cloned"] > 0 and want_res["split_sources"] > 0
