@@ -79,6 +79,12 @@ _SIGS = {
     "fgs_adam_step_peers": (C.c_int, [_i64, _i32, _i32, C.POINTER(_p), C.POINTER(_p), _p, _p, _i32,
                                       C.POINTER(_i64), C.POINTER(_f), _f, _f, _f, _i32, _i32, _p]),
     "fgs_set_exchange_grid": (C.c_int, [_i32]),
+    "fgs_adam_step_gathered": (C.c_int, [_i64, _i32, C.POINTER(_p), _p, _p, _p, _i32,
+                                         C.POINTER(_i64), C.POINTER(_f), _f, _f, _f, _i32, _i32, _p]),
+    "fgs_preprocess_backward_push": (C.c_int, [C.POINTER(PreprocessParams)] + [_p] * 11
+                                     + [_i32, _i64, C.POINTER(_p), _p, _p]),
+    "fgs_adam_step_owner": (C.c_int, [_i64, _i32, _i32, C.POINTER(_p), _p, _p, _p, _p, _i32,
+                                      C.POINTER(_i64), C.POINTER(_f), _f, _f, _f, _i32, _i32, _p]),
     "fgs_metric_map": (C.c_int, [_i64, _p, _p, _f, _p, _p, _p, _p]),
     "fgs_score_accumulate": (C.c_int, [_i64, _p, _p, _i64, _p, _p, _p]),
     "fgs_score_finalize": (C.c_int, [_i64, _p, _p, _i32, _p, _p, _p, _p]),

@@ -442,6 +442,11 @@ struct PbwdArgs {
   float *ap, *am, *av;
   float lr[6];
   float b1, b2, eps, bc1, bc2;
+  // push mode (kPush): no Adam; the staged gradients
+  // are added into the owning rank's gradient buffer instead (rank r owns flat
+  // elements [r shard, (r + 1) shard); peer_g[r] is rank r's buffer base)
+  int64_t shard;
+  float* peer_g[8];
 };
 
 // Shared-memory staging of the register-held gradients in the fused Adam
@@ -508,11 +513,49 @@ __device__ __forceinline__ void adam_block(const PbwdArgs& a, int64_t seg, int w
   }
 }
 
+__device__ __forceinline__ void red_add_sys(float* dst, float v) {
+  asm volatile("red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(dst), "f"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_sys4(float* dst, float4 v) {
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Push mode: adds the CTA's staged gradients of one attribute segment (the
+// contiguous flat run [seg + base * width, + cnt * width)) into the buffer of
+// the rank that owns each element, over NVLink for the other ranks' shards:
+// 16-byte vector reductions on 4-float boundaries of the flat index (a shard
+// is a multiple of 4 floats, so no vector crosses two owners), scalar ones for
+// the ragged head and tail.
+__device__ __forceinline__ void push_block(const PbwdArgs& a, int64_t seg, int width, int base,
+                                           int cnt, const float* sgrad) {
+  const int64_t g0 = seg + (int64_t)base * width;
+  const int count = cnt * width;
+  const int head = min(count, (int)((4 - (g0 & 3)) & 3));
+  const int body4 = (count - head) / 4;
+  const int tail0 = head + 4 * body4;
+  const int t = threadIdx.x;
+  if (t < head || (t >= 32 && t - 32 < count - tail0)) {
+    const int k = t < head ? t : tail0 + (t - 32);
+    const int64_t g = g0 + k;
+    red_add_sys(a.peer_g[g / a.shard] + g, sgrad[k]);
+  }
+  for (int j = t; j < body4; j += kPreThreads) {
+    const int k = head + 4 * j;
+    const int64_t g = g0 + k;
+    red_add_sys4(a.peer_g[g / a.shard] + g,
+                 make_float4(sgrad[k], sgrad[k + 1], sgrad[k + 2], sgrad[k + 3]));
+  }
+}
+
 __device__ __forceinline__ v3 v3s(float s, v3 a) { return V3(s * a.x, s * a.y, s * a.z); }
 __device__ __forceinline__ v3 v3sr(v3 a, float s) { return V3(a.x * s, a.y * s, a.z * s); }
 __device__ __forceinline__ v3 v3add(v3 a, v3 b) { return V3(a.x + b.x, a.y + b.y, a.z + b.z); }
 
-template <bool kTrain, bool kAdam>
+// kPush (with kAdam's staging): the gradients go to their owning ranks instead
+// of an Adam step (fgs_preprocess_backward_push)
+template <bool kTrain, bool kAdam, bool kPush = false>
 __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a) {
   extern __shared__ float s_buf[];  // [kPreThreads * S3]: staged sh, overwritten by dsh
   const fgs_preprocess_params& P = a.p;
@@ -896,7 +939,18 @@ __global__ void __launch_bounds__(kPreThreads) preprocess_bwd_kernel(PbwdArgs a)
     }
     __syncthreads();
     float* gdst = dsh_dst + (int64_t)base * S3;
-    if (kAdam) {
+    if constexpr (kPush) {
+      const int64_t n = P.n;
+      const float* sg = s_buf + kPreThreads * S3;
+      push_block(a, 0, 3, base, cnt, sg + kAdamMeans * kPreThreads);
+      push_block(a, 3 * n, 3, base, cnt, sg + kAdamDc * kPreThreads);
+      push_block(a, 6 * n, S3, base, cnt, s_dsh);
+      push_block(a, 51 * n, 1, base, cnt, sg + kAdamLogit * kPreThreads);
+      push_block(a, 52 * n, 3, base, cnt, sg + kAdamScale * kPreThreads);
+      push_block(a, 55 * n, 4, base, cnt, sg + kAdamRot * kPreThreads);
+      // the reductions reach the other GPUs before the caller's barrier
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+    } else if (kAdam) {
       const int64_t n = P.n;
       const float* sg = s_buf + kPreThreads * S3;
       adam_block(a, 0, 3, base, cnt, sg + kAdamMeans * kPreThreads, a.lr[0]);
@@ -1181,6 +1235,57 @@ int fgs_preprocess_backward_train(const fgs_preprocess_params* p, const float* p
   const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
   preprocess_bwd_kernel<true, false><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
   return check_launch("preprocess_backward_train");
+}
+
+int fgs_preprocess_backward_push(const fgs_preprocess_params* p, const float* params,
+                                 const float* viewmatrix, const float* projmatrix,
+                                 const float* cam_pos, const float* cov3d_fwd,
+                                 const float* dL_drgb, const float* dL_dxys,
+                                 const float* dL_dconic_opacity, const float* dL_dviewspace,
+                                 const int32_t* radii, const uint8_t* clamped, int32_t world,
+                                 int64_t shard, float* const* grad_ranks, float* stats,
+                                 void* stream) {
+  int st = validate_pre(p);
+  if (st) return st;
+  if (p->n == 0) return FGS_OK;
+  FGS_CHECK_ARG(!p->use_cov3d_precomp && !p->use_colors_precomp,
+                "training mode needs the scales+quats and dc+sh paths");
+  FGS_CHECK_ARG(p->max_sh_coeffs == 15, "training mode stores 15 SH rest coefficients");
+  FGS_CHECK_ARG(world >= 1 && world <= 8, "world must be in [1, 8]");
+  FGS_CHECK_ARG(shard > 0 && shard % 4 == 0 && shard * world >= 59 * (int64_t)p->n,
+                "shard must be a positive multiple of 4 with world * shard >= 59 n");
+  FGS_CHECK_ARG(params && viewmatrix && projmatrix && cam_pos && cov3d_fwd && dL_drgb && dL_dxys &&
+                    dL_dconic_opacity && dL_dviewspace && radii && clamped && grad_ranks && stats,
+                "missing pointer");
+  FGS_CHECK_ARG(FGS_ALIGNED(dL_dconic_opacity, 16) && FGS_ALIGNED(dL_dviewspace, 16),
+                "conic and viewspace gradients must be 16-byte aligned");
+  const int64_t n = p->n;
+  PbwdArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int r = 0; r < world; ++r) {
+    FGS_CHECK_ARG(grad_ranks[r] && FGS_ALIGNED(grad_ranks[r], 16),
+                  "gradient buffer of rank %d missing or not 16-byte aligned", r);
+    a.peer_g[r] = grad_ranks[r];
+  }
+  a.p = *p;
+  a.focal_x = 0.5f * (float)p->image_width / (p->tan_fovx < 1e-6f ? 1e-6f : p->tan_fovx);
+  a.focal_y = 0.5f * (float)p->image_height / (p->tan_fovy < 1e-6f ? 1e-6f : p->tan_fovy);
+  a.raw = params;
+  a.means3d = params; a.sh = params + 6 * n; a.vm = viewmatrix; a.pm = projmatrix;
+  a.cam_pos = cam_pos; a.cov3d_fwd = cov3d_fwd;
+  a.drgb = dL_drgb; a.dxys = dL_dxys; a.dconic = dL_dconic_opacity; a.dvs_out = dL_dviewspace;
+  a.radii = radii; a.clamped = clamped;
+  a.st_acc = stats;
+  a.st_acc_abs = stats + n;
+  a.st_denom = stats + 2 * n;
+  a.st_max_radii = stats + 3 * n;
+  a.shard = shard;
+  const size_t smem = (size_t)kPreThreads * (p->max_sh_coeffs * 3 + kAdamStaged) * sizeof(float);
+  static unsigned long long attr_done = 0;
+  if (smem > 48 * 1024) smem_attr_once(preprocess_bwd_kernel<true, true, true>, (int)smem, &attr_done);
+  const int blocks = (int)((n + kPreThreads - 1) / kPreThreads);
+  preprocess_bwd_kernel<true, true, true><<<blocks, kPreThreads, smem, (cudaStream_t)stream>>>(a);
+  return check_launch("preprocess_backward_push");
 }
 
 int fgs_preprocess_backward_adam(const fgs_preprocess_params* p, const float* viewmatrix,

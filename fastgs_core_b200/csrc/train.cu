@@ -484,7 +484,7 @@ struct PeerPtrs {
 constexpr int kPeerUnroll = 2;
 
 __global__ void __launch_bounds__(256)
-    adam_peers_kernel(int64_t n4, int world, int rank, PeerPtrs pp, float* __restrict__ m,
+    adam_peers_kernel(int64_t n4, int world, int rank, int nstore, PeerPtrs pp, float* __restrict__ m,
                       float* __restrict__ v, AdamGroups grp, float b1, float b2, float eps,
                       float bc1, float bc2) {
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -516,10 +516,51 @@ __global__ void __launch_bounds__(256)
       adam4(p4, mm, vv, gg[u], 4 * i4, grp, b1, b2, eps, bc1, bc2);
       reinterpret_cast<float4*>(m)[i4] = mm;
       reinterpret_cast<float4*>(v)[i4] = vv;
-      for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(pp.p[r])[i4] = p4;
+      for (int r = 0; r < nstore; ++r) reinterpret_cast<float4*>(pp.p[r])[i4] = p4;
     }
   }
   // make the stores to the peers visible system-wide before the caller's barrier
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// ------------------------------------------- Adam of a pushed gradient shard
+// The ranks have already added their gradients into the owner's buffer
+// (fgs_preprocess_backward_push): the owner reads its summed shard, clears it
+// for the next step, applies Adam and stores the new parameters into every
+// rank's copy (peer stores, or one multimem.st when params_mc is given).
+__global__ void __launch_bounds__(256)
+    adam_owner_kernel(int64_t n4, int world, int rank, PeerPtrs pp, float* p_mc,
+                      float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
+                      AdamGroups grp, float b1, float b2, float eps, float bc1, float bc2) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float4* g4 = reinterpret_cast<float4*>(g);
+  for (int64_t base = t; base < n4; base += stride * kPeerUnroll) {
+    float4 gg[kPeerUnroll], p4[kPeerUnroll], mm[kPeerUnroll], vv[kPeerUnroll];
+#pragma unroll
+    for (int u = 0; u < kPeerUnroll; ++u) {
+      const int64_t i4 = base + u * stride;
+      if (i4 >= n4) continue;
+      gg[u] = __ldcg(g4 + i4);
+      p4[u] = reinterpret_cast<const float4*>(pp.p[rank])[i4];
+      mm[u] = reinterpret_cast<float4*>(m)[i4];
+      vv[u] = reinterpret_cast<float4*>(v)[i4];
+    }
+#pragma unroll
+    for (int u = 0; u < kPeerUnroll; ++u) {
+      const int64_t i4 = base + u * stride;
+      if (i4 >= n4) break;
+      g4[i4] = make_float4(0.f, 0.f, 0.f, 0.f);
+      adam4(p4[u], mm[u], vv[u], gg[u], 4 * i4, grp, b1, b2, eps, bc1, bc2);
+      reinterpret_cast<float4*>(m)[i4] = mm[u];
+      reinterpret_cast<float4*>(v)[i4] = vv[u];
+      if (p_mc) {
+        mc_store(p_mc + 4 * i4, p4[u]);
+      } else {
+        for (int r = 0; r < world; ++r) reinterpret_cast<float4*>(pp.p[r])[i4] = p4[u];
+      }
+    }
+  }
   asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
@@ -797,10 +838,104 @@ int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, float* const
   const int64_t want = (n4 + 255) / 256;
   const int64_t cap = (int64_t)sms * (g_exchange_bps > 0 ? g_exchange_bps : 8);
   const int blocks = (int)(want < cap ? want : cap);
-  adam_peers_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(n4, world, rank, pp, exp_avg,
+  adam_peers_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(n4, world, rank, world, pp, exp_avg,
                                                               exp_avg_sq, g, beta1, beta2, eps,
                                                               bc1, bc2);
   return check_launch("adam_step_peers");
+}
+
+int fgs_adam_step_gathered(int64_t shard, int32_t world, const float* const* grads,
+                           float* params, float* exp_avg, float* exp_avg_sq, int32_t num_groups,
+                           const int64_t* group_end, const float* group_lr, float beta1,
+                           float beta2, float eps, int32_t step, int32_t bias_correction,
+                           void* stream) {
+  FGS_CHECK_ARG(shard >= 0 && shard % 4 == 0, "shard length must be a multiple of 4");
+  FGS_CHECK_ARG(world >= 1 && world <= kMaxPeers, "world must be in [1, %d]", kMaxPeers);
+  FGS_CHECK_ARG(num_groups >= 1 && num_groups <= 8, "num_groups must be in [1, 8]");
+  FGS_CHECK_ARG(group_end && group_lr && grads, "missing pointer table");
+  if (shard == 0) return FGS_OK;
+  FGS_CHECK_ARG(params && exp_avg && exp_avg_sq, "missing pointer");
+  PeerPtrs pp;
+  memset(&pp, 0, sizeof(pp));
+  uintptr_t align = (uintptr_t)params | (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq;
+  for (int r = 0; r < world; ++r) {
+    FGS_CHECK_ARG(grads[r], "missing gradient pointer %d", r);
+    pp.g[r] = grads[r];
+    align |= (uintptr_t)grads[r];
+  }
+  pp.p[0] = params;
+  FGS_CHECK_ARG(align % 16 == 0, "buffers must be 16-byte aligned");
+  AdamGroups g;
+  memset(&g, 0, sizeof(g));
+  g.count = num_groups;
+  for (int k = 0; k < num_groups; ++k) {
+    g.end[k] = group_end[k];
+    g.lr[k] = group_lr[k];
+  }
+  float bc1 = 1.f, bc2 = 1.f;
+  if (bias_correction) {
+    FGS_CHECK_ARG(step >= 1, "step must be >= 1 with bias correction");
+    bc1 = 1.0f / (1.0f - powf(beta1, (float)step));
+    bc2 = 1.0f / (1.0f - powf(beta2, (float)step));
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n4 = shard / 4;
+  const int64_t want = (n4 + 255) / 256;
+  const int64_t cap = (int64_t)sms * (g_exchange_bps > 0 ? g_exchange_bps : 8);
+  const int blocks = (int)(want < cap ? want : cap);
+  adam_peers_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(n4, world, 0, 1, pp, exp_avg,
+                                                              exp_avg_sq, g, beta1, beta2, eps,
+                                                              bc1, bc2);
+  return check_launch("adam_step_gathered");
+}
+
+int fgs_adam_step_owner(int64_t shard, int32_t world, int32_t rank, float* const* params_ranks,
+                        float* params_mc, float* grads, float* exp_avg, float* exp_avg_sq,
+                        int32_t num_groups, const int64_t* group_end, const float* group_lr,
+                        float beta1, float beta2, float eps, int32_t step, int32_t bias_correction,
+                        void* stream) {
+  FGS_CHECK_ARG(shard >= 0 && shard % 4 == 0, "shard length must be a multiple of 4");
+  FGS_CHECK_ARG(world >= 1 && world <= kMaxPeers && rank >= 0 && rank < world,
+                "world must be in [1, %d] and rank in [0, world)", kMaxPeers);
+  FGS_CHECK_ARG(num_groups >= 1 && num_groups <= 8, "num_groups must be in [1, 8]");
+  FGS_CHECK_ARG(group_end && group_lr && params_ranks, "missing pointer table");
+  if (shard == 0) return FGS_OK;
+  FGS_CHECK_ARG(grads && exp_avg && exp_avg_sq, "missing pointer");
+  PeerPtrs pp;
+  memset(&pp, 0, sizeof(pp));
+  uintptr_t align = (uintptr_t)grads | (uintptr_t)exp_avg | (uintptr_t)exp_avg_sq | (uintptr_t)params_mc;
+  for (int r = 0; r < world; ++r) {
+    FGS_CHECK_ARG(params_ranks[r], "missing parameter pointer for rank %d", r);
+    pp.p[r] = params_ranks[r];
+    align |= (uintptr_t)params_ranks[r];
+  }
+  FGS_CHECK_ARG(align % 16 == 0, "buffers must be 16-byte aligned");
+  AdamGroups g;
+  memset(&g, 0, sizeof(g));
+  g.count = num_groups;
+  for (int k = 0; k < num_groups; ++k) {
+    g.end[k] = group_end[k];
+    g.lr[k] = group_lr[k];
+  }
+  float bc1 = 1.f, bc2 = 1.f;
+  if (bias_correction) {
+    FGS_CHECK_ARG(step >= 1, "step must be >= 1 with bias correction");
+    bc1 = 1.0f / (1.0f - powf(beta1, (float)step));
+    bc2 = 1.0f / (1.0f - powf(beta2, (float)step));
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t n4 = shard / 4;
+  const int64_t want = (n4 + 255) / 256;
+  const int64_t cap = (int64_t)sms * (g_exchange_bps > 0 ? g_exchange_bps : 8);
+  const int blocks = (int)(want < cap ? want : cap);
+  adam_owner_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(n4, world, rank, pp, params_mc, grads,
+                                                              exp_avg, exp_avg_sq, g, beta1, beta2,
+                                                              eps, bc1, bc2);
+  return check_launch("adam_step_owner");
 }
 
 int fgs_adam_step_multicast(int64_t shard, const float* params_local, float* params_mc,

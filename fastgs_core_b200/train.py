@@ -81,6 +81,11 @@ def _symmetric_pair(numel: int, dev, group, multicast: bool = True):
             symm.enable_symm_mem_for_group(name)
         p = symm.empty(numel, dtype=torch.float32, device=dev)
         g = symm.empty(numel, dtype=torch.float32, device=dev)
+        # zeroed before any rank can see them: with the push exchange, peers
+        # add into this gradient buffer from their first backward pass on
+        p.zero_()
+        g.zero_()
+        torch.cuda.synchronize(dev)
         hp = symm.rendezvous(p, name)
         hg = symm.rendezvous(g, name)
         if multicast and (not getattr(hp, "multicast_ptr", 0) or not getattr(hg, "multicast_ptr", 0)):
@@ -194,7 +199,7 @@ class Trainer:
         self._symm = None
         if self.world > 1:
             self.comm = comm or os.environ.get("FGS_COMM", "") or default_comm(self.world)
-            if self.comm in ("multicast", "p2p"):
+            if self.comm in ("multicast", "p2p", "push", "ce"):
                 self._symm = _symmetric_pair(padded, d, process_group, self.comm == "multicast")
                 if self._symm is None:
                     self.comm = "nccl"
@@ -311,7 +316,7 @@ class Trainer:
         self._per = -(-total // (4 * self.world)) * 4
         padded = self._per * self.world
         self._symm = None
-        if self.comm in ("multicast", "p2p"):
+        if self.comm in ("multicast", "p2p", "push", "ce"):
             self._symm = _symmetric_pair(padded, d, self.pg, self.comm == "multicast")
             if self._symm is None:
                 self.comm = "nccl"
@@ -368,6 +373,66 @@ class Trainer:
         for off, ln in ((0, rs), (rs, re - rs), (re, per - re)):
             ends = np.clip(shard_ends - off, 0, ln)
             self._pieces.append((off, ln, (C.c_int64 * 6)(*ends.tolist())))
+        if self.comm == "ce":
+            self._ce_setup(shard_ends)
+
+    def _ce_setup(self, shard_ends) -> None:
+        """Copy-engine exchange state: views of every rank's symmetric
+        buffers, a staging buffer for the other ranks' gradient shards, the
+        pull and push streams, and the shard's chunks (each with its group
+        table) that the pipeline moves one by one."""
+        world, per, d = self.world, self._per, self.dev
+        padded = per * world
+        self._peer_g = [self._hg.get_buffer(r, (padded,), torch.float32) for r in range(world)]
+        self._peer_p = [self._hp.get_buffer(r, (padded,), torch.float32) for r in range(world)]
+        self._stage = torch.empty((max(world - 1, 1), per), device=d)
+        if not hasattr(self, "_pull"):
+            self._pull = torch.cuda.Stream(device=d)
+            self._push = torch.cuda.Stream(device=d)
+            self._ce_start, self._ce_done = torch.cuda.Event(), torch.cuda.Event()
+        chunks = max(1, int(os.environ.get("FGS_CE_CHUNKS", "4")))
+        step = -(-per // (4 * chunks)) * 4
+        self._ce_chunks = []
+        for off in range(0, per, step):
+            ln = min(step, per - off)
+            ends = np.clip(shard_ends - off, 0, ln)
+            self._ce_chunks.append((off, ln, (C.c_int64 * 6)(*ends.tolist()),
+                                    torch.cuda.Event(), torch.cuda.Event()))
+
+    def _ce_exchange(self, lrs, b1, b2) -> None:
+        """Reduce-scatter + Adam + all-gather over the copy engines, chunk by
+        chunk: the pull stream copies the other ranks' gradients of a chunk of
+        this rank's shard into the staging buffer, this stream runs Adam on it
+        (gradients summed in rank order), the push stream copies the chunk's
+        new parameters into every other rank's buffer; the three overlap
+        across chunks."""
+        world, rank, lo = self.world, self.rank, self._lo
+        main = torch.cuda.current_stream(self.dev)
+        others = [r for r in range(world) if r != rank]
+        self._ce_start.record(main)
+        self._pull.wait_event(self._ce_start)
+        self._push.wait_event(self._ce_start)
+        for off, ln, ends, ev_in, ev_adam in self._ce_chunks:
+            a, b = lo + off, lo + off + ln
+            with torch.cuda.stream(self._pull):
+                for k, r in enumerate(others):
+                    self._stage[k, off:off + ln].copy_(self._peer_g[r][a:b], non_blocking=True)
+                ev_in.record(self._pull)
+            main.wait_event(ev_in)
+            gp = []
+            for r in range(world):
+                gp.append(_p(self.grads_pad[a:]) if r == rank else _p(self._stage[others.index(r), off:]))
+            gpa = (C.c_void_p * world)(*[g.value for g in gp])
+            self._call("adam", lib().fgs_adam_step_gathered, ln, world, gpa, _p(self.params_pad[a:]),
+                       _p(self.exp_avg[off:]), _p(self.exp_avg_sq[off:]), 6, ends, lrs, b1, b2,
+                       self.eps, self.step_count, int(self.bias_correction), self._stream())
+            ev_adam.record(main)
+            with torch.cuda.stream(self._push):
+                self._push.wait_event(ev_adam)
+                for r in others:
+                    self._peer_p[r][a:b].copy_(self.params_pad[a:b], non_blocking=True)
+        self._ce_done.record(self._push)
+        main.wait_event(self._ce_done)
 
     def _exchange(self, off, length, group_end, lrs, b1, b2):
         """Fused exchange + Adam of shard elements [off, off + length)."""
@@ -673,6 +738,14 @@ class Trainer:
                        float(self.betas[0]), float(self.betas[1]), self.eps, self.step_count,
                        int(self.bias_correction), _p(self.step_stats if stats is None else stats), st)
             return img
+        if self.comm == "push":
+            # the gradients go straight into their owners' buffers
+            gp = (C.c_void_p * self.world)(*self._hg.buffer_ptrs)
+            self._call("preprocess_backward_train", L.fgs_preprocess_backward_push, C.byref(prm),
+                       _p(self.params), _p(vm), _p(pm), _p(cp), _p(cov3d), _p(dcolors),
+                       _p(dmeans2d), _p(dconic), _p(dvs), _p(radii), _p(clamped), self.world,
+                       self._per, gp, _p(self.step_stats), st)
+            return img
         self._call("preprocess_backward_train", L.fgs_preprocess_backward_train, C.byref(prm),
                    _p(self.params), _p(vm), _p(pm), _p(cp), _p(cov3d), _p(dcolors), _p(dmeans2d),
                    _p(dconic), _p(dvs), _p(radii), _p(clamped), int(bool(accumulate)),
@@ -762,7 +835,7 @@ class Trainer:
                              fused_adam=True, stats=self.stats)
             return 1
         self.step_stats.zero_()
-        if not mine:
+        if not mine and self.comm != "push":
             self.grads.zero_()
         for j, v in enumerate(mine):
             lo = None
@@ -777,6 +850,28 @@ class Trainer:
         lr = self.lrs
         lrs = (C.c_float * 6)(lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations)
         b1, b2 = float(self.betas[0]), float(self.betas[1])
+        if self.comm == "ce":
+            ev = self._begin("exchange")
+            self._hp.barrier(channel=0)
+            self._ce_exchange(lrs, b1, b2)
+            self._hp.barrier(channel=1)
+            self._end("exchange", ev)
+            return len(mine)
+        if self.comm == "push":
+            # every rank's gradients pushed -> the owner's Adam on its summed
+            # shard, which clears it and stores the parameters to every rank
+            ev = self._begin("exchange")
+            self._hp.barrier(channel=0)
+            world, lo = self.world, self._lo
+            pp = (C.c_void_p * world)(*[self._hp.buffer_ptrs[r] + 4 * lo for r in range(world)])
+            mc = getattr(self._hp, "multicast_ptr", 0) if world > 2 else 0
+            self._call("adam", lib().fgs_adam_step_owner, self._per, world, self.rank, pp,
+                       C.c_void_p(mc + 4 * lo) if mc else None, _p(self.grads_pad[lo:]),
+                       _p(self.exp_avg), _p(self.exp_avg_sq), 6, self._group_end, lrs, b1, b2,
+                       self.eps, self.step_count, int(self.bias_correction), self._stream())
+            self._hp.barrier(channel=1)
+            self._end("exchange", ev)
+            return len(mine)
         if self.comm in ("multicast", "p2p"):
             # every rank's gradients written -> fused exchange + Adam -> every
             # rank's parameter broadcast landed (also guards the next step's

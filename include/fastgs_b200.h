@@ -475,6 +475,47 @@ FGS_API int fgs_adam_step_peers(int64_t shard, int32_t world, int32_t rank, floa
                                 const float* group_lr, float beta1, float beta2, float eps,
                                 int32_t step, int32_t bias_correction, void* stream);
 
+/* Data-parallel exchange by pushing (new here; the reference is single-
+ * device). Rank r owns the flat elements [r shard, (r + 1) shard) of the
+ * gradient buffer; grad_ranks[r] (host array of `world` pointers) addresses
+ * rank r's whole buffer in this process (symmetric memory or peer mappings).
+ * fgs_preprocess_backward_push: fgs_preprocess_backward_train whose gradients
+ *   are added (relaxed system-scope float reductions, 16-byte vectors where the
+ *   flat index allows) into the owner's buffer, which must hold zeros or
+ *   earlier views' sums of this step; the densification statistics update
+ *   locally as in fgs_preprocess_backward_train.
+ * fgs_adam_step_owner: after a cross-rank barrier, the owner reads its summed
+ *   shard `grads` (local), writes zeros back for the next step, applies the
+ *   Adam rule of fgs_adam_step to its moments and stores the new parameters
+ *   into every rank's copy: params_ranks[r] (this rank's shard in rank r's
+ *   buffer), or one multimem.st to params_mc when that multicast address is
+ *   given. A second barrier publishes them. Group ends relative to the shard. */
+FGS_API int fgs_preprocess_backward_push(const fgs_preprocess_params* p, const float* params,
+                                         const float* viewmatrix, const float* projmatrix,
+                                         const float* cam_pos, const float* cov3d_fwd,
+                                         const float* dL_drgb, const float* dL_dxys,
+                                         const float* dL_dconic_opacity,
+                                         const float* dL_dviewspace, const int32_t* radii,
+                                         const uint8_t* clamped, int32_t world, int64_t shard,
+                                         float* const* grad_ranks, float* stats, void* stream);
+FGS_API int fgs_adam_step_owner(int64_t shard, int32_t world, int32_t rank,
+                                float* const* params_ranks, float* params_mc, float* grads,
+                                float* exp_avg, float* exp_avg_sq, int32_t num_groups,
+                                const int64_t* group_end, const float* group_lr, float beta1,
+                                float beta2, float eps, int32_t step, int32_t bias_correction,
+                                void* stream);
+
+/* Adam of a gathered gradient shard (new here): grads[r] (host array of
+ * `world` pointers, local memory, e.g. this rank's own gradients and copies of
+ * the other ranks' shards brought over by the copy engines) are summed in
+ * rank order, as fgs_adam_step_peers sums them, and the Adam rule of
+ * fgs_adam_step updates params / exp_avg / exp_avg_sq (shard floats). */
+FGS_API int fgs_adam_step_gathered(int64_t shard, int32_t world, const float* const* grads,
+                                   float* params, float* exp_avg, float* exp_avg_sq,
+                                   int32_t num_groups, const int64_t* group_end,
+                                   const float* group_lr, float beta1, float beta2, float eps,
+                                   int32_t step, int32_t bias_correction, void* stream);
+
 /* Grid budget of fgs_adam_step_multicast and fgs_adam_step_peers for the
  * launches that follow in this process: at most blocks_per_sm CTAs of 256
  * threads per SM (0 restores their defaults of 4 and 8). Both kernels stride

@@ -3,7 +3,8 @@ that renders both views itself:
 
 * one step at the real Adam epsilon (1e-8), every exchange (the NVLink
   multicast kernel fgs_adam_step_multicast, the peer kernel
-  fgs_adam_step_peers, and NCCL reduce-scatter / all-gather): the Adam moments agree within the float-atomic noise of the
+  fgs_adam_step_peers, the push exchange fgs_preprocess_backward_push +
+  fgs_adam_step_owner, the copy-engine pipeline around fgs_adam_step_gathered, and NCCL reduce-scatter / all-gather): the Adam moments agree within the float-atomic noise of the
   gradients; the parameter update agrees where the gradient stands out of
   that noise (elsewhere Adam's normalised step of a near-zero gradient takes
   either sign, and the test bounds it by the learning rate); the
@@ -147,7 +148,7 @@ def _rel(a, b):
     return float((a - b).abs().max() / max(float(b.abs().max()), 1e-30))
 
 
-@pytest.mark.parametrize("comm", ["multicast", "p2p", "nccl"])
+@pytest.mark.parametrize("comm", ["multicast", "p2p", "push", "ce", "nccl"])
 def test_two_rank_step_matches_single_process(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -174,7 +175,8 @@ def test_two_rank_step_matches_single_process(comm):
     assert big.float().mean() > 0.3
 
 
-@pytest.mark.parametrize("comm", ["multicast", "p2p", "nccl", "multicast+overlap", "p2p+overlap"])
+@pytest.mark.parametrize("comm", ["multicast", "p2p", "push", "ce", "nccl", "multicast+overlap",
+                                  "p2p+overlap"])
 def test_two_rank_densify_matches_single_process(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
