@@ -3,6 +3,7 @@ reference's layout, loaded back."""
 import json
 
 import numpy as np
+import pytest
 from PIL import Image
 
 from fastgs_core_b200 import dataset as DS
@@ -50,3 +51,55 @@ def test_prepare_dataset(tmp_path):
     scene = DS.init_scene(points, colors, 3)
     assert scene.features_rest.shape == (50, 15, 3)
     np.testing.assert_allclose(scene.features_dc * 0.28209479177387814 + 0.5, colors, atol=1e-6)
+
+
+def _golden_case(tag, tmp_path):
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "dataset_ref.npz"))
+    pre = f"{tag}/file/"
+    for k in z.files:
+        if k.startswith(pre):
+            (tmp_path / k[len(pre):]).write_bytes(z[k].tobytes())
+    return z
+
+
+# the keyword arguments tests/golden/make_dataset_golden.py gave the reference's prepare_dataset
+_GOLDEN_KW = {
+    "plain": dict(width=32, height=24, max_frames=120, frame_step=1, start_index=0, max_points=0,
+                  seed=42, extra_points_ratio=0.0, extra_points_mode="surface-jitter",
+                  extra_points_jitter_scale=0.01),
+    "jitter": dict(width=40, height=30, max_frames=2, frame_step=2, start_index=1, max_points=90,
+                   seed=7, extra_points_ratio=0.5, extra_points_mode="surface-jitter",
+                   extra_points_jitter_scale=0.02),
+    "bbox": dict(width=64, height=48, max_frames=120, frame_step=1, start_index=0, max_points=0,
+                 seed=3, extra_points_ratio=0.25, extra_points_mode="bbox",
+                 extra_points_jitter_scale=0.01),
+}
+
+
+@pytest.mark.parametrize("tag", sorted(_GOLDEN_KW))
+def test_prepare_dataset_matches_reference_loader(tag, tmp_path):
+    """The loader against the reference's own prepare_dataset / init_model run
+    on the same capture (tests/golden/make_dataset_golden.py): frame selection,
+    axis change and normalisation, subsampling and extra points from the same
+    seeded draws, cameras, resized targets and the initial parameters."""
+    z = _golden_case(tag, tmp_path)
+    kw = dict(_GOLDEN_KW[tag])
+    w, h = kw.pop("width"), kw.pop("height")
+    cams, targets, points, colors, base = DS.prepare_dataset(tmp_path, w, h, **kw)
+    assert base == int(z[f"{tag}/base"]) and len(cams) == int(z[f"{tag}/ncams"])
+    np.testing.assert_array_equal(points, z[f"{tag}/points"])
+    np.testing.assert_array_equal(colors, z[f"{tag}/colors"])
+    for i, c in enumerate(cams):
+        p = f"{tag}/cam{i}/"
+        np.testing.assert_array_equal(np.asarray(c.viewmatrix, np.float32), z[p + "viewmatrix"])
+        np.testing.assert_array_equal(np.asarray(c.projmatrix, np.float32), z[p + "projmatrix"])
+        np.testing.assert_array_equal(np.asarray(c.campos, np.float32).reshape(-1),
+                                      z[p + "campos"].reshape(-1))
+        assert (c.tan_fovx, c.tan_fovy) == tuple(z[p + "tan"])
+        assert (c.width, c.height) == tuple(z[p + "size"])
+        np.testing.assert_allclose(targets[i], z[p + "target"], rtol=0, atol=1e-6)
+    scene = DS.init_scene(points, colors, 3)
+    for k in ("means3d", "features_dc", "features_rest", "opacity_logits", "log_scales", "rotations"):
+        np.testing.assert_array_equal(np.asarray(getattr(scene, k), np.float32), z[f"{tag}/init/{k}"])
