@@ -94,3 +94,22 @@ def test_spz_round_trip(tmp_path):
     sh_a, sh_b = a["sh"].reshape(500, -1), b["sh"].reshape(500, -1)
     assert np.abs(sh_b[:, :9] - np.clip(sh_a[:, :9], -1, 127 / 128)).max() <= 4.5 / 128
     assert np.abs(sh_b[:, 9:] - np.clip(sh_a[:, 9:], -1, 127 / 128)).max() <= 8.5 / 128
+
+
+def test_spz_cloud_matches_reference_exporter():
+    """spz_cloud_arrays against what the reference's own save_as_spz hands to
+    spz.GaussianCloud for the same model (tests/golden/make_export_golden.py):
+    app-frame positions, raw log-scales, axis-conjugated rotations of the
+    normalised quaternions, logits, dc and rest coefficients."""
+    import os
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "export_ref.npz"))
+    params = {k[3:]: z[k] for k in z.files if k.startswith("in/")}
+    got = E.spz_cloud_arrays(params)
+    for k in ("positions", "scales", "alphas", "colors", "sh"):
+        np.testing.assert_array_equal(got[k], z["cloud/" + k].astype(np.float32), err_msg=k)
+    # a quaternion and its negation are the same rotation
+    q, w = got["rotations"].reshape(-1, 4), z["cloud/rotations"].reshape(-1, 4)
+    sgn = np.where((q * w).sum(1, keepdims=True) < 0, -1.0, 1.0)
+    np.testing.assert_allclose(q * sgn, w, rtol=0, atol=2e-6)
+    assert int(z["cloud/sh_degree"]) == 3
