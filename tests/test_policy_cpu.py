@@ -40,3 +40,26 @@ def test_sample_camera_indices_matches_numpy():
     b = np.random.default_rng(3).choice(20, size=10, replace=False)
     assert np.array_equal(a, b)
     assert sample_camera_indices(np.random.default_rng(3), 4, 10).size == 4
+
+
+def test_learning_rates_match_reference_policy():
+    """OptimizerPolicy.learning_rates against the reference's own
+    ScannerFastGSOptimizerPolicy (update_learning_rate + apply_gradients,
+    recorded by tests/golden/make_policy_golden.py) over sampled iterations
+    0..36000 in two configurations: every group's rate, -1 where it does not
+    step."""
+    import os
+
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    from make_policy_golden import CONFIGS
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "policy_ref.npz"))
+    for tag, kw in CONFIGS.items():
+        pol = OptimizerPolicy(OptimizerPolicyConfig(**kw))
+        want = z[f"{tag}/lrs"]
+        for r, it in enumerate(z["iterations"]):
+            lr = pol.learning_rates(int(it))
+            got = [lr.means, lr.dc, lr.rest, lr.opacity, lr.scales, lr.rotations]
+            np.testing.assert_allclose(got, want[r], rtol=1e-12, atol=0, err_msg=f"{tag} {it}")
