@@ -893,6 +893,15 @@ class Trainer:
                 self._exchange(rest[0], rest[1], rest[2], lrs, b1, b2)
                 check(lib().fgs_set_exchange_grid(0), "set_exchange_grid")
                 self._hp.barrier(channel=2)
+            elif lr.rest < 0.0:
+                # the SH rest group does not step (the reference's cadence,
+                # scripts/train_scanner_fastgs.py:166-171, steps it every 16th
+                # iteration at most): its gradients are dropped, as there, so
+                # only the other parts of the shard cross NVLink
+                front, _, back = self._pieces
+                self._exchange(front[0], front[1], front[2], lrs, b1, b2)
+                self._exchange(back[0], back[1], back[2], lrs, b1, b2)
+                self._hp.barrier(channel=1)
             else:
                 self._exchange(0, self._per, self._group_end, lrs, b1, b2)
                 self._hp.barrier(channel=1)

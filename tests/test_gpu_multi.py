@@ -92,6 +92,7 @@ def _worker(rank, port, comm, mode, eps, q):
     # "<comm>+overlap": the SH exchange overlapped with the next render's geometry
     comm, _, ov = comm.partition("+")
     os.environ["FGS_OVERLAP_EXCHANGE"] = "1" if ov == "overlap" else "0"
+    freeze = ov == "freeze"  # "<comm>+freeze": the SH rest group does not step
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
@@ -99,6 +100,8 @@ def _worker(rank, port, comm, mode, eps, q):
     try:
         scene, cams, tg = _setup()
         tr = Trainer(scene, dev, process_group=dist.group.WORLD, comm=comm, eps=eps)
+        if freeze:
+            tr.lrs.rest = -1.0
         targets = [torch.from_numpy(t).to(dev) if k == rank else None for k, t in enumerate(tg)]
         res = _run(tr, cams, targets, mode)
         torch.cuda.synchronize()
@@ -125,12 +128,14 @@ def _spawn(comm, mode, eps):
     return out
 
 
-def _single(mode, eps):
+def _single(mode, eps, freeze=False):
     from fastgs_core_b200.train import Trainer
 
     scene, cams, tg = _setup()
     dev = torch.device("cuda", 0)
     tr = Trainer(scene, dev, eps=eps)
+    if freeze:
+        tr.lrs.rest = -1.0
     targets = [torch.from_numpy(t).to(dev) for t in tg]
     res = _run(tr, cams, targets, mode)
     torch.cuda.synchronize()
@@ -195,3 +200,27 @@ def test_two_rank_densify_matches_single_process(comm):
         assert _rel(m, want_m) < 1e-3 and _rel(v, want_v) < 1e-3, r
         assert _rel(s, want_s) < 1e-3, r
     assert torch.equal(res[0][3], res[1][3])  # replicas agree exactly
+
+
+@pytest.mark.parametrize("comm", ["multicast", "p2p"])
+def test_two_rank_step_with_frozen_sh_group(comm):
+    """A step in which the SH rest group does not step (the reference's
+    cadence): the exchange moves only the other parts of the shard; the SH
+    coefficients and their moments stay as they were, the rest follows the
+    single process."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _spawn(comm + "+freeze", "step", 1.0)
+    if res[0][1] != comm:
+        pytest.skip("symmetric memory (NVLink multicast / peer mappings) unavailable on this box")
+    _, _, (_, n, want_p, want_m, want_v, _) = _single("step", 1.0, freeze=True)
+    scene = _setup()[0]
+    p0 = torch.from_numpy(np.concatenate([getattr(scene, k).ravel() for k in (
+        "means3d", "features_dc", "features_rest", "opacity_logits", "log_scales", "rotations")]))
+    for r in range(2):
+        _, _, _, p, m, v, _ = res[r]
+        assert torch.equal(p[6 * n:51 * n], p0[6 * n:51 * n]), r
+        assert not bool(m[6 * n:51 * n].any()) and not bool(v[6 * n:51 * n].any()), r
+        assert _rel(p, want_p) < 1e-5, (r, _rel(p, want_p))
+        assert _rel(m, want_m) < 1e-4 and _rel(v, want_v) < 1e-4, r
+    assert torch.equal(res[0][3], res[1][3])
