@@ -72,7 +72,8 @@ __device__ __forceinline__ void splat_rows(float y, float a, float b, float c, f
 // warp-level row culling and the loop are shared by PX pixels. The per-pixel
 // arithmetic is unchanged (bit-identical results).
 template <int PX, bool kMask, bool kMetric>
-// six resident CTAs per SM (config 3: 0.646 ms; four: 0.662 ms)
+// six resident CTAs per SM (config 3: 0.646 ms; four: 0.662 ms; seven, at 32
+// registers with spills: 0.647 ms)
 __global__ void __launch_bounds__(kTile / PX, 6) raster_fwd_kernel(FwdArgs a) {
   constexpr int kThreads = kTile / PX;
   constexpr int kWarpRows = 2 * PX;

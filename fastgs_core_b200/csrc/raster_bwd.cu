@@ -219,6 +219,8 @@ constexpr int kBwdMaskPx = 2;
 constexpr int kGroupBuckets = kChunk / 32;
 
 template <int PX, bool kMask>
+// no occupancy cap: 48 registers (capping at 40 / 32 for 12 / 14 CTAs per SM
+// spills and measured 10% / 20% slower on config 3)
 __global__ void __launch_bounds__(kTilePx / PX) raster_bwd_kernel(BwdArgs a) {
   constexpr int kThreads = kTilePx / PX;
   constexpr int kWarpRows = 2 * PX;
